@@ -1,0 +1,563 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 deformable-sampling hot path (DCNv2 / MSDA forward).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
+
+Headline workload: DCNv2 forward of the BEVFormer
+ResNet-101-DCN stage-4 conv2 -- 6 cameras x 512 -> 512 channels, 29 x 50, 3x3,
+stride 1, pad 1, NHWC fp16 with fp32 accumulation, offsets ~N(0, 2^2) px,
+mask = sigmoid(N(0, 1)).  A step is one forward over one 6-camera batch; each
+rank runs its own batch (cameras sharded by rank, no collective on the data
+path), so scaling is weak and ``value`` is the aggregate TFLOP/s of all ranks.
+
+Timing: W untimed warm-up steps, then exactly K steps replayed from a CUDA
+graph and timed with CUDA events on the launching stream, bracketed by a
+barrier and cuda.synchronize(); the max over ranks is reported.  Inputs rotate
+through enough independent sets that the working set exceeds the 126 MB L2,
+so no step finds its inputs in L2 from the step before.  SM clocks and clock
+event reasons are sampled through NVML during the timed region.
+
+Also reported on the same line: ``e2e`` (the same metric through the public
+``modulated_deform_conv2d`` call with inputs copied from pinned host memory and
+the output copied back every step), the roofline of the fused kernel against
+MEASURED_PEAKS.json, the CPU oracle timed on a bounded sample (rank 0, N = 1)
+and, in ``secondary``, BASELINE configs 3 (DCN bf16), 4 and 5 (MSDA fp32).
+
+``--impl reference`` times the reference algorithm on the host cores instead
+(the CPU oracle restatement in oracle/, all threads) on the same workload and
+metric; under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "bev-kernels_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "DCNv2 fwd TFLOP/s & MSDA fwd µs/call on B200, as % of roofline"
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+DCN_CFGS = {
+    "cfg2": dict(B=6, C=512, H=29, W=50, Cout=512, dtype="float16", big=0.0,
+                 desc="DCNv2 stage-4 conv2 fwd: 6x512->512, 29x50, 3x3 s1 p1, NHWC fp16"),
+    "cfg3": dict(B=6, C=256, H=58, W=100, Cout=256, dtype="bfloat16", big=0.05,
+                 desc="DCNv2 stage-3 conv2 fwd: 6x256->256, 58x100, 3x3 s1 p1, NHWC bf16, "
+                      "5% offsets at +-(H+4)"),
+}
+MSDA_CFGS = {
+    "cfg4": dict(B=2, shapes=[(200, 200)], M=8, C=32, Q=40000, P=4, oob=0.02,
+                 desc="MSDA TSA fwd: bs 2, 1 level 200x200, 8x32, Q=40000, P=4, fp32"),
+    "cfg5": dict(B=6, shapes=[(116, 200), (58, 100), (29, 50), (15, 25)], M=8, C=32, Q=10000,
+                 P=8, oob=0.0,
+                 desc="MSDA SCA fwd: 6 cams, 4 levels, 8x32, Q=10000, P=8, fp32"),
+}
+
+
+# ----------------------------------------------------------------------------- helpers
+def _peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def _traffic(key):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary, or None."""
+    path = os.path.join(REPO, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(key)
+    except (OSError, ValueError):
+        return None
+
+
+def _out(n, pad, dil, k, stride):
+    return (n + 2 * pad - (dil * (k - 1) + 1)) // stride + 1
+
+
+def dcn_work(cfg):
+    """Algorithmic FLOPs and unique bytes of one DCN forward (SURVEY 8(d) definitions)."""
+    B, C, H, W, Co = cfg["B"], cfg["C"], cfg["H"], cfg["W"], cfg["Cout"]
+    Ho, Wo = _out(H, 1, 1, 3, 1), _out(W, 1, 1, 3, 1)
+    flops = 2.0 * B * Ho * Wo * Co * C * 9
+    e = 2  # fp16 / bf16
+    nbytes = e * (B * C * H * W + Co * C * 9 + B * 18 * Ho * Wo + B * 9 * Ho * Wo + B * Co * Ho * Wo)
+    return flops, nbytes
+
+
+def msda_bytes(cfg):
+    B, M, C, Q, P = cfg["B"], cfg["M"], cfg["C"], cfg["Q"], cfg["P"]
+    L = len(cfg["shapes"])
+    S = sum(h * w for h, w in cfg["shapes"])
+    return 4 * (B * S * M * C + B * Q * M * L * P * 2 + B * Q * M * L * P + B * Q * M * C)
+
+
+class ClockSampler:
+    """Polls SM clock and clock-event reasons through NVML in a thread."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        self._period = period_s
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: report nothing rather than guess
+            self._nv = None
+
+    def _sample(self):
+        nv = self._nv
+        mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+        try:
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        except AttributeError:
+            bits = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+        self.samples.append(mhz)
+        for bit, name in self.REASONS.items():
+            if bits & bit:
+                self.reasons.add(name)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+            if not self.samples:
+                self._sample()
+
+    def summary(self):
+        if self._nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        busy = [s for s in self.samples]
+        return {"sm_mhz": statistics.median(busy) if busy else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons - {"gpu_idle"}),
+                "samples": len(busy)}
+
+
+# ----------------------------------------------------------------------------- data
+def dcn_sets(cfg, n_sets, seed, img0, device):
+    """n_sets independent input sets; camera b of a set is generated from
+    (seed, global image index img0 + b) so any rank can regenerate its shard."""
+    import torch
+    from bevk.sharding import image_seed
+    dt = getattr(torch, cfg["dtype"])
+    B, C, H, W, Co = cfg["B"], cfg["C"], cfg["H"], cfg["W"], cfg["Cout"]
+    sets = []
+    for s in range(n_sets):
+        g = torch.Generator(device=device)
+        xs, offs, masks = [], [], []
+        for b in range(B):
+            g.manual_seed(image_seed(seed, img0 + b, s))
+            xs.append(torch.randn(1, C, H, W, generator=g, device=device))
+            off = torch.randn(1, 18, H, W, generator=g, device=device) * 2.0
+            if cfg["big"]:
+                sel = torch.rand(off.shape, generator=g, device=device) < cfg["big"]
+                sign = torch.where(torch.rand(off.shape, generator=g, device=device) < 0.5,
+                                   -1.0, 1.0)
+                off = torch.where(sel, sign * (H + 4), off)
+            offs.append(off)
+            masks.append(torch.sigmoid(torch.randn(1, 9, H, W, generator=g, device=device)))
+        g.manual_seed(seed * 7919 + s)
+        w = torch.randn(Co, C, 3, 3, generator=g, device=device) * math.sqrt(2.0 / (C * 9))
+        x = torch.cat(xs).to(dt).contiguous(memory_format=torch.channels_last)
+        out = torch.empty(B, Co, H, W, dtype=dt, device=device, memory_format=torch.channels_last)
+        sets.append(dict(x=x, off=torch.cat(offs).to(dt), mask=torch.cat(masks).to(dt),
+                         w=w.to(dt), out=out))
+    return sets
+
+
+def msda_sets(cfg, n_sets, seed, device):
+    import torch
+    sets = []
+    B, M, C, Q, P = cfg["B"], cfg["M"], cfg["C"], cfg["Q"], cfg["P"]
+    shapes = cfg["shapes"]
+    L = len(shapes)
+    sizes = [h * w for h, w in shapes]
+    lsi = [0]
+    for s in sizes[:-1]:
+        lsi.append(lsi[-1] + s)
+    for s in range(n_sets):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 31 + s)
+        value = torch.randn(B, sum(sizes), M, C, generator=g, device=device)
+        loc = torch.rand(B, Q, M, L, P, 2, generator=g, device=device)
+        if cfg["oob"]:
+            sel = torch.rand(B, Q, M, L, P, 1, generator=g, device=device) < cfg["oob"]
+            loc = torch.where(sel, loc * 1.4 - 0.2, loc)
+        attn = torch.softmax(torch.randn(B, Q, M, L * P, generator=g, device=device), -1)
+        sets.append(dict(value=value, loc=loc, attn=attn.view(B, Q, M, L, P),
+                         shapes=torch.tensor(shapes, dtype=torch.int64, device=device),
+                         lsi=torch.tensor(lsi, dtype=torch.int64, device=device)))
+    return sets
+
+
+def n_sets_for(set_bytes, lo=2, hi=16):
+    return max(lo, min(hi, math.ceil(2 * L2_BYTES / max(set_bytes, 1))))
+
+
+# ----------------------------------------------------------------------------- timing
+def graph_time(step_fns, steps, warmup, stream, clocks=None, dist=None):
+    """Warm up, capture `steps` launches (cycling step_fns) in CUDA graphs, replay them
+    once between events; returns (elapsed_ms max over ranks, launches)."""
+    import torch
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            step_fns[i % len(step_fns)]()
+    torch.cuda.synchronize()
+    chunk = min(steps, 1024)
+    graphs = []
+    done = 0
+    while done < steps:
+        n = min(chunk, steps - done)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                step_fns[(done + i) % len(step_fns)]()
+        graphs.append(g)
+        done += n
+    # one untimed replay so graph upload is outside the timed region
+    with torch.cuda.stream(stream):
+        graphs[0].replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ctx = clocks if clocks is not None else _Null()
+    with ctx:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for g in graphs:
+                g.replay()
+            end.record(stream)
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    del graphs
+    return _max_over_ranks(ms, dist)
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def _max_over_ranks(v, dist):
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- workloads
+def bench_dcn(cfg_name, steps, warmup, device, seed, img0, stream, dist=None, clocks=None):
+    import _modulated_deform_conv_ext as ext
+    import modulated_deform_conv as mdc
+    cfg = DCN_CFGS[cfg_name]
+    flops, nbytes = dcn_work(cfg)
+    n_sets = n_sets_for(nbytes)
+    sets = dcn_sets(cfg, n_sets, seed, img0, device)
+    for s in sets:
+        s["wpk"] = mdc.packed_weight(s["w"])
+
+    def make(s):
+        return lambda: ext.dcn_forward(s["x"], s["off"], s["mask"], s["wpk"], None, s["out"],
+                                       3, 3, 1, 1, 1, 1, 1, 1, 1, 1, False)
+
+    ms = graph_time([make(s) for s in sets], steps, warmup, stream, clocks, dist)
+    per_launch_s = ms / 1e3 / steps
+    return dict(ms=ms, flops=flops, bytes=nbytes, per_launch_s=per_launch_s, n_sets=n_sets,
+                sets=sets)
+
+
+def bench_dcn_e2e(cfg_name, steps, warmup, device, sets, stream, clocks=None, dist=None):
+    """Public-API end-to-end: pinned host inputs -> device, modulated_deform_conv2d,
+    output -> pinned host, every step."""
+    import torch
+    import modulated_deform_conv as mdc
+    cfg = DCN_CFGS[cfg_name]
+    s0 = sets[0]
+    hx = s0["x"].cpu().pin_memory()                   # keeps channels_last strides
+    ho = s0["off"].cpu().pin_memory()
+    hm = s0["mask"].cpu().pin_memory()
+    w = s0["w"]
+    dx = torch.empty_like(s0["x"])
+    do = torch.empty_like(s0["off"])
+    dm = torch.empty_like(s0["mask"])
+    B, Co, H, W = cfg["B"], cfg["Cout"], cfg["H"], cfg["W"]
+    hout = torch.empty(B, Co, H, W, dtype=s0["x"].dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (hx, ho, hm))
+    d2h = hout.numel() * hout.element_size()
+
+    def step():
+        dx.copy_(hx, non_blocking=True)
+        do.copy_(ho, non_blocking=True)
+        dm.copy_(hm, non_blocking=True)
+        y = mdc.modulated_deform_conv2d(dx, do, dm, w, None, 1, 1, 1)
+        hout.copy_(y, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            step()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ctx = clocks if clocks is not None else _Null()
+    with ctx:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(steps):
+                step()
+            end.record(stream)
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ms = _max_over_ranks(start.elapsed_time(end), dist)
+    return ms, h2d, d2h
+
+
+def bench_msda(cfg_name, steps, warmup, device, seed, stream):
+    import _ms_deform_attn_ext as ext
+    cfg = MSDA_CFGS[cfg_name]
+    nbytes = msda_bytes(cfg)
+    sets = msda_sets(cfg, n_sets_for(nbytes, lo=2, hi=4), seed, device)
+
+    def make(s):
+        return lambda: ext.forward(s["value"], s["shapes"], s["lsi"], s["loc"], s["attn"], 64,
+                                   False)
+
+    ms = graph_time([make(s) for s in sets], steps, warmup, stream)
+    return dict(ms=ms, bytes=nbytes, per_launch_s=ms / 1e3 / steps, n_sets=len(sets))
+
+
+# ----------------------------------------------------------------------------- CPU legs
+def cpu_dcn_sample(cfg_name, target_s, seed):
+    """Time the CPU oracle on a bounded pixel range of the workload (all host threads).
+    Returns (TFLOP/s, pixels per call, calls, threads)."""
+    import numpy as np
+    import torch
+    from oracle import oracle
+    cfg = DCN_CFGS[cfg_name]
+    s = dcn_sets(cfg, 1, seed, 0, torch.device("cpu"))[0]
+    x = s["x"].float().contiguous().numpy()
+    off, mask, w = (s[k].float().contiguous().numpy() for k in ("off", "mask", "w"))
+    B, C, H, W, Co = cfg["B"], cfg["C"], cfg["H"], cfg["W"], cfg["Cout"]
+    M = B * H * W
+    per_px = 2.0 * Co * C * 9
+    t0 = time.perf_counter()
+    oracle.dcn_forward(x, off, mask, w, None, 1, 1, 1, pix_range=(0, 256))
+    t_px = max((time.perf_counter() - t0) / 256, 1e-7)
+    npix = int(min(M, max(256, target_s / t_px)))
+    times = []
+    for r in range(3):
+        lo = (r * npix) % max(1, M - npix + 1)
+        t0 = time.perf_counter()
+        oracle.dcn_forward(x, off, mask, w, None, 1, 1, 1, pix_range=(lo, lo + npix))
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return per_px * npix / t / 1e12, npix, len(times), oracle.max_threads()
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm (oracle port) on the host cores."""
+    from oracle import oracle
+    import torch
+    cfg = DCN_CFGS["cfg2"]
+    s = dcn_sets(cfg, 1, 2026, 0, torch.device("cpu"))[0]
+    x = s["x"].float().contiguous().numpy()
+    off, mask, w = (s[k].float().contiguous().numpy() for k in ("off", "mask", "w"))
+    B, C, H, W, Co = cfg["B"], cfg["C"], cfg["H"], cfg["W"], cfg["Cout"]
+    M = B * H * W
+    per_px = 2.0 * Co * C * 9
+    t0 = time.perf_counter()
+    oracle.dcn_forward(x, off, mask, w, None, 1, 1, 1, pix_range=(0, 128))
+    t_px = max((time.perf_counter() - t0) / 128, 1e-7)
+    budget_s = 90.0
+    npix = int(min(M, max(64, budget_s / (args.steps + args.warmup) / t_px)))
+    for i in range(args.warmup):
+        oracle.dcn_forward(x, off, mask, w, None, 1, 1, 1, pix_range=(0, npix))
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        lo = (i * npix) % max(1, M - npix + 1)
+        oracle.dcn_forward(x, off, mask, w, None, 1, 1, 1, pix_range=(lo, lo + npix))
+    el = time.perf_counter() - t0
+    value = per_px * npix * args.steps / el / 1e12
+    threads = oracle.max_threads()
+    sample = (f"{npix} of {M} output pixels of cfg2 per step (C oracle, fp32 math, "
+              f"double accumulation, {threads} OpenMP threads)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE cfg2 "
+        "distributions)",
+        "config": {"workload": cfg["desc"], "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args)
+        return
+
+    import datetime
+    import torch
+    import torch.distributed as dist_mod
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                    device_id=device)
+        dist = dist_mod
+    stream = torch.cuda.Stream(device=device)
+    peaks, peaks_src = _peaks()
+    seed = 2026
+
+    # headline: cfg2 DCN, this rank's 6 cameras are global images [6*rank, 6*rank+6)
+    clocks = ClockSampler(local_rank)
+    cfg_name = "cfg2"
+    cfg = DCN_CFGS[cfg_name]
+    res = bench_dcn(cfg_name, args.steps, args.warmup, device, seed, cfg["B"] * rank, stream,
+                    dist, clocks)
+    flops, nbytes = res["flops"], res["bytes"]
+    ms = res["ms"]
+    value = world * flops * args.steps / (ms / 1e3) / 1e12
+    achieved = flops / res["per_launch_s"] / 1e12
+    roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+            "traffic": _traffic("dcn_fwd_tc cfg2"),
+            "peak_source": f"{peaks_src} bf16_tflops (burst; kernel timed alone)",
+            "algorithmic_bytes": nbytes,
+            "hbm_frac": nbytes / res["per_launch_s"] / 1e9 / peaks["hbm_gbs"]}
+
+    e2e_clocks = ClockSampler(local_rank)
+    e2e_ms, h2d, d2h = bench_dcn_e2e(cfg_name, args.steps, args.warmup, device, res["sets"],
+                                     stream, e2e_clocks, dist)
+    e2e_value = world * flops * args.steps / (e2e_ms / 1e3) / 1e12
+    del res["sets"]
+    torch.cuda.empty_cache()
+
+    secondary = {}
+    if not args.no_secondary:
+        k2 = min(args.steps, 500)
+        r3 = bench_dcn("cfg3", k2, args.warmup, device, seed + 1, cfg["B"] * rank, stream)
+        del r3["sets"]
+        a3 = r3["flops"] / r3["per_launch_s"] / 1e12
+        secondary["dcn_cfg3"] = {"workload": DCN_CFGS["cfg3"]["desc"],
+                                 "us_per_call": r3["per_launch_s"] * 1e6,
+                                 "tflops": a3, "frac_tensor_peak": a3 / peaks["bf16_tflops"],
+                                 "traffic": _traffic("dcn_fwd_tc cfg3")}
+        torch.cuda.empty_cache()
+        for name in ("cfg4", "cfg5"):
+            r = bench_msda(name, k2, args.warmup, device, seed + 2, stream)
+            gbs = r["bytes"] / r["per_launch_s"] / 1e9
+            secondary[f"msda_{name}"] = {
+                "workload": MSDA_CFGS[name]["desc"], "us_per_call": r["per_launch_s"] * 1e6,
+                "algorithmic_GBps": gbs, "frac_hbm_peak": gbs / peaks["hbm_gbs"],
+                "roofline_us": r["bytes"] / (peaks["hbm_gbs"] * 1e9) * 1e6,
+                "traffic": _traffic(f"msda_fwd {name}")}
+            torch.cuda.empty_cache()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, npix, calls, threads = cpu_dcn_sample(cfg_name, 3.5, seed)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"C oracle (oracle/bevk_oracle.c) on {npix} of "
+                         f"{cfg['B'] * cfg['H'] * cfg['W']} output pixels of cfg2, median of "
+                         f"{calls} calls, fp32 math with double accumulation"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded; BASELINE cfg2 shapes and distributions)",
+            "config": {"workload": cfg["desc"] + " (fp32 accumulate)",
+                       "global_batch": cfg["B"] * world, "parallelism": f"dp{world} "
+                       "(cameras sharded across ranks, no collective on the data path)",
+                       "l2": f"inputs rotate over {res['n_sets']} independent sets "
+                             f"({res['n_sets'] * nbytes / 2**20:.0f} MiB > 126 MB L2)"},
+            "roofline": roof,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "api": "modulated_deform_conv.modulated_deform_conv2d (pinned host in/out)",
+                    "clocks": e2e_clocks.summary()},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,127 @@
+"""ctypes binding of the C ABI in ``include/bevk.h`` (``libbevk.so``).
+
+This is the binding a Python caller without the torch extensions would use,
+and the one the GPU parity tests call through.  Pointers are plain integers
+(e.g. ``tensor.data_ptr()``); streams are raw ``cudaStream_t`` handles
+(e.g. ``torch.cuda.current_stream().cuda_stream``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import LIB_PATH, _BUILD_HINT
+
+DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_F64 = 0, 1, 2, 3
+
+OK = 0
+ERR_INVALID_ARGUMENT = -1
+ERR_UNSUPPORTED = -2
+ERR_INDEX_OVERFLOW = -3
+ERR_MISALIGNED = -4
+ERR_CUDA = -5
+ERR_WORKSPACE = -6
+ERR_DEVICE_TIMEOUT = -7
+
+# Every exported symbol of include/bevk.h.
+EXPORTED_SYMBOLS = (
+    "bevk_version",
+    "bevk_status_string",
+    "bevk_last_error_message",
+    "bevk_device_watchdog",
+    "bevk_dcn_output_size",
+    "bevk_dcn_packed_weight_bytes",
+    "bevk_dcn_pack_weight",
+    "bevk_dcn_forward_workspace_bytes",
+    "bevk_dcn_forward",
+    "bevk_modulated_deformable_im2col",
+    "bevk_modulated_deformable_im2col_opt",
+    "bevk_modulated_deformable_im2col_nhwc",
+    "bevk_ms_deform_attn_forward",
+)
+
+
+class DcnProblem(ctypes.Structure):
+    """Mirror of ``bevk_dcn_problem``."""
+
+    _fields_ = [
+        ("dtype", ctypes.c_int),
+        ("batch", ctypes.c_int), ("in_channels", ctypes.c_int),
+        ("height", ctypes.c_int), ("width", ctypes.c_int),
+        ("out_channels", ctypes.c_int), ("kernel_h", ctypes.c_int), ("kernel_w", ctypes.c_int),
+        ("stride_h", ctypes.c_int), ("stride_w", ctypes.c_int),
+        ("pad_h", ctypes.c_int), ("pad_w", ctypes.c_int),
+        ("dilation_h", ctypes.c_int), ("dilation_w", ctypes.c_int),
+        ("groups", ctypes.c_int), ("deformable_groups", ctypes.c_int),
+        ("input_strides", ctypes.c_int64 * 4),
+        ("offset_strides", ctypes.c_int64 * 4),
+        ("mask_strides", ctypes.c_int64 * 4),
+        ("output_strides", ctypes.c_int64 * 4),
+        ("mask_is_logit", ctypes.c_int),
+        ("has_bias", ctypes.c_int),
+    ]
+
+
+class BevkError(RuntimeError):
+    def __init__(self, status: int, what: str, detail: str):
+        super().__init__(f"{what}: {status_string(status)} ({status}): {detail}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib():
+    """Load libbevk.so and declare argument types (idempotent)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise OSError(f"{LIB_PATH} not found; {_BUILD_HINT}")
+    L = ctypes.CDLL(LIB_PATH)
+    i, vp, sz, i64p = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int64)
+    pp = ctypes.POINTER(DcnProblem)
+    L.bevk_version.restype = i
+    L.bevk_status_string.restype = ctypes.c_char_p
+    L.bevk_status_string.argtypes = [i]
+    L.bevk_last_error_message.restype = ctypes.c_char_p
+    L.bevk_device_watchdog.restype = i
+    L.bevk_device_watchdog.argtypes = [i, ctypes.POINTER(ctypes.c_uint)]
+    L.bevk_dcn_output_size.restype = i
+    L.bevk_dcn_output_size.argtypes = [pp, ctypes.POINTER(i), ctypes.POINTER(i)]
+    L.bevk_dcn_packed_weight_bytes.restype = sz
+    L.bevk_dcn_packed_weight_bytes.argtypes = [pp]
+    L.bevk_dcn_pack_weight.restype = i
+    L.bevk_dcn_pack_weight.argtypes = [pp, vp, vp, vp]
+    L.bevk_dcn_forward_workspace_bytes.restype = sz
+    L.bevk_dcn_forward_workspace_bytes.argtypes = [pp]
+    L.bevk_dcn_forward.restype = i
+    L.bevk_dcn_forward.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp, sz, vp]
+    col_args = [vp, vp, vp] + [i] * 15
+    L.bevk_modulated_deformable_im2col.restype = i
+    L.bevk_modulated_deformable_im2col.argtypes = col_args + [vp, i, vp]
+    L.bevk_modulated_deformable_im2col_opt.restype = i
+    L.bevk_modulated_deformable_im2col_opt.argtypes = col_args + [vp, i, vp]
+    L.bevk_modulated_deformable_im2col_nhwc.restype = i
+    L.bevk_modulated_deformable_im2col_nhwc.argtypes = col_args + [i, vp, i, vp]
+    L.bevk_ms_deform_attn_forward.restype = i
+    L.bevk_ms_deform_attn_forward.argtypes = [vp, i64p, i64p, vp, vp] + [i] * 8 + [vp, i, vp]
+    _lib = L
+    return L
+
+
+def status_string(status: int) -> str:
+    return lib().bevk_status_string(int(status)).decode()
+
+
+def last_error() -> str:
+    return lib().bevk_last_error_message().decode()
+
+
+def check(status: int, what: str) -> None:
+    if status != OK:
+        raise BevkError(status, what, last_error())
+
+
+def version() -> int:
+    return int(lib().bevk_version())

@@ -1,0 +1,90 @@
+// bevk_internal.h -- host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+
+#include "bevk.h"
+
+namespace bevk {
+
+// Records a formatted message for bevk_last_error_message() and returns
+// `status` so call sites can `return fail(BEVK_ERR_..., "...")`.
+int fail(int status, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+void clear_error();
+const char *last_error();
+
+// Maps a CUDA error from the most recent launch into a status.
+int check_launch(const char *what);
+
+// Cached per-device properties (filled once per device, thread-safe).
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  int max_smem_optin = 0;
+  int l2_bytes = 0;
+};
+const DeviceInfo &device_info(int device);
+int current_device();
+
+inline size_t dtype_size(int dtype) {
+  switch (dtype) {
+    case BEVK_DTYPE_F32: return 4;
+    case BEVK_DTYPE_F16: return 2;
+    case BEVK_DTYPE_BF16: return 2;
+    case BEVK_DTYPE_F64: return 8;
+    default: return 0;
+  }
+}
+
+inline bool aligned(const void *p, size_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+// Derived geometry of a DCN problem (validated).
+struct DcnDims {
+  int B, Cin, H, W, Cout, kH, kW, T;
+  int sh, sw, ph, pw, dh, dw, groups, dg;
+  int Ho, Wo;
+  int Cin_g, Cout_g, Cin_g_pad, cpdg;
+  int64_t M;  // B*Ho*Wo
+};
+int dcn_dims(const bevk_dcn_problem *p, DcnDims *d);
+
+// Kernel launchers (return BEVK_OK or a status; arguments are pre-validated).
+int launch_msda_forward(const void *value, const int64_t *shapes, const int64_t *lsi,
+                        const void *loc, const void *attn, int B, int S, int heads,
+                        int C, int L, int Q, int P, void *out, int dtype,
+                        cudaStream_t stream);
+
+int launch_dcn_pack_weight(const DcnDims &d, const void *w, void *wpk, int dtype,
+                           cudaStream_t stream);
+int launch_nchw_to_nhwc(const void *src, void *dst, int B, int C, int H, int W,
+                        const int64_t src_strides[4], int dtype, cudaStream_t stream);
+int launch_dcn_forward_simt(const bevk_dcn_problem *p, const DcnDims &d,
+                            const void *x, const void *off, const void *msk,
+                            const void *wpk, const void *bias, void *out,
+                            cudaStream_t stream);
+// Tensor-core path: x must be channel-contiguous (c stride 1) with 16-byte
+// aligned pixel rows; returns BEVK_ERR_UNSUPPORTED when the geometry is not
+// covered so the caller can pick the SIMT kernel.
+bool dcn_tc_supported(const bevk_dcn_problem *p, const DcnDims &d);
+int launch_dcn_forward_tc(const bevk_dcn_problem *p, const DcnDims &d,
+                          const void *x, const int64_t x_strides[4],
+                          const void *off, const void *msk, const void *wpk,
+                          const void *bias, void *out, cudaStream_t stream);
+
+// Column-matrix ops.  col_layout 0: [C*T, B*Ho*Wo] (row c*T + t);
+// col_layout 1: [B*Ho*Wo, T*C] (k = t*C + c).
+int launch_dcn_im2col(const bevk_dcn_problem *p, const DcnDims &d, const void *x,
+                      const void *off, const void *msk, void *col, int col_layout,
+                      cudaStream_t stream);
+
+// Device watchdog word (one per device, defined in dcn_tc.cu).
+int read_and_clear_watchdog(int device, unsigned int *code);
+
+}  // namespace bevk

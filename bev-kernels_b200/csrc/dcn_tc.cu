@@ -1,0 +1,532 @@
+// dcn_tc.cu -- fused DCNv2 forward on the sm_100a tensor cores (tcgen05/TMEM).
+//
+// out[m, co] = bias[co] + sum_{t, c} A[m, (t, c)] * W[co, t, c]
+// A[m, (t, c)] = mask(m, t) * bilinear(x[b(m)], p(m) + tap(t) + offset(m, t))[c]
+//
+// One CTA computes a 128-pixel x BN-output-channel tile.  The reduction runs
+// over (tap, 64-channel chunk) stages:
+//   * 8 gather warps build the A stage in shared memory directly in the
+//     canonical K-major 128-byte-swizzled UMMA layout: 8 lanes cover one
+//     pixel's 64 channels (16-byte vector loads from NHWC input, one load per
+//     bilinear corner), interpolate (packed half2 FMA for fp16, fp32 FMA for
+//     bf16, as the reference's fp32 math would round), and st.shared the
+//     result -- the column matrix never touches HBM;
+//   * 1 TMA warp streams the matching [BN x 64] tile of the packed weights
+//     ([Cout][tap][Cin_pad], K-major, 128-byte swizzle) into shared memory;
+//   * 1 MMA warp allocates the TMEM accumulator and issues, from one thread,
+//     tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) x 4 per stage,
+//     committing each stage back to its "empty" barrier;
+//   * the 8 gather warps then drain TMEM (tcgen05.ld 32x32b), add bias and
+//     store fp16/bf16 to any output layout.
+// Pipelining uses full/empty mbarrier rings.  Every wait is bounded (2 s);
+// a wait that gives up records its site in g_bevk_watchdog, raises a CTA-wide
+// abort flag so the other roles unwind, and the CTA still frees its TMEM.
+//
+// The per-(pixel, tap) geometry (corner base offset + four corner weights with
+// the mask folded in) is computed once per tile into shared memory; offset and
+// mask tensors may have any strides (NCHW as in
+// ModulatedDeformConv2dFunction, NHWC / fused logits as in
+// DCNSplitNHWCFunction), matching csrc/modulated_deform_conv_cuda_kernel.cuh
+// :403-470 and csrc/dcn_fused_nhwc_kernel.cuh:85-194 semantics.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "bevk_internal.h"
+#include "bevk_ptx.cuh"
+
+namespace bevk {
+
+// Device watchdog word: set by a bounded wait that expired (see bevk.h).
+__device__ unsigned int g_bevk_watchdog = 0;
+
+namespace {
+
+constexpr int kBM = 128;           // pixels per tile (UMMA M)
+constexpr int kBK = 64;            // channels per stage (128 B of fp16/bf16)
+constexpr int kGatherWarps = 8;
+constexpr int kThreads = (kGatherWarps + 2) * 32;
+constexpr int kTmaWarp = kGatherWarps;
+constexpr int kMmaWarp = kGatherWarps + 1;
+constexpr int kMaxTaps = 9;
+
+// Watchdog sites (low byte) -- identify which wait expired.
+enum : unsigned int {
+  kSiteGatherEmpty = 0xB0C1,
+  kSiteTmaEmpty = 0xB0C2,
+  kSiteMmaFull = 0xB0C3,
+  kSiteEpilogue = 0xB0C4,
+};
+
+struct TcParams {
+  int Cin, H, W, Ho, Wo, Cout, kW, T;
+  int sh, sw, ph, pw, dh, dw;
+  int M, Cin_pad, n_cc, n_k, n_tiles_n, tap_major;
+  int mask_is_logit, has_bias;
+  int xs0, xs2, xs3;        // input strides (channel stride is 1)
+  int64_t os[4], ms[4], ys[4];
+};
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kA = 0;
+  static constexpr int kB = kA + STAGES * kABytes;
+  static constexpr int kGW = kB + STAGES * kBBytes;          // uint4 weights [T][BM]
+  static constexpr int kGB = kGW + kMaxTaps * kBM * 16;      // int base offsets [T][BM]
+  static constexpr int kBar = kGB + kMaxTaps * kBM * 4;      // full_a[S], full_b[S], empty[S], tmem_full
+  static constexpr int kMisc = kBar + (3 * STAGES + 1) * 8;  // tmem slot, abort flag
+  static constexpr int kTotal = kMisc + 16;
+  static constexpr int kAlloc = kTotal + 1024;               // 1024-byte alignment slack
+};
+
+template <typename T>
+struct GatherMath;
+
+// fp16: weights as half2 (w, w); packed half2 FMA chain.
+template <>
+struct GatherMath<__half> {
+  static constexpr uint32_t kFmt = 0;
+  __device__ static uint32_t pack_weight(float w) {
+    __half2 h = __float2half2_rn(w);
+    return *reinterpret_cast<uint32_t *>(&h);
+  }
+  __device__ static uint32_t lerp2(uint4 w, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    const __half2 r0 = __hmul2(*reinterpret_cast<const __half2 *>(&w.x),
+                               *reinterpret_cast<const __half2 *>(&a));
+    const __half2 r1 = __hfma2(*reinterpret_cast<const __half2 *>(&w.y),
+                               *reinterpret_cast<const __half2 *>(&b), r0);
+    const __half2 r2 = __hfma2(*reinterpret_cast<const __half2 *>(&w.z),
+                               *reinterpret_cast<const __half2 *>(&c), r1);
+    __half2 r3 = __hfma2(*reinterpret_cast<const __half2 *>(&w.w),
+                         *reinterpret_cast<const __half2 *>(&d), r2);
+    return *reinterpret_cast<uint32_t *>(&r3);
+  }
+  __device__ static uint16_t store_bits(float v) {
+    __half h = __float2half_rn(v);
+    return *reinterpret_cast<uint16_t *>(&h);
+  }
+};
+
+// bf16: weights as fp32; interpolate in fp32 and round once.
+template <>
+struct GatherMath<__nv_bfloat16> {
+  static constexpr uint32_t kFmt = 1;
+  __device__ static uint32_t pack_weight(float w) { return __float_as_uint(w); }
+  __device__ static uint32_t lerp2(uint4 w, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    const float w0 = __uint_as_float(w.x), w1 = __uint_as_float(w.y);
+    const float w2 = __uint_as_float(w.z), w3 = __uint_as_float(w.w);
+    float lo = w0 * __uint_as_float(a << 16);
+    float hi = w0 * __uint_as_float(a & 0xFFFF0000u);
+    lo = fmaf(w1, __uint_as_float(b << 16), lo);
+    hi = fmaf(w1, __uint_as_float(b & 0xFFFF0000u), hi);
+    lo = fmaf(w2, __uint_as_float(c << 16), lo);
+    hi = fmaf(w2, __uint_as_float(c & 0xFFFF0000u), hi);
+    lo = fmaf(w3, __uint_as_float(d << 16), lo);
+    hi = fmaf(w3, __uint_as_float(d & 0xFFFF0000u), hi);
+    __nv_bfloat162 r = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&r);
+  }
+  __device__ static uint16_t store_bits(float v) {
+    __nv_bfloat16 h = __float2bfloat16_rn(v);
+    return *reinterpret_cast<uint16_t *>(&h);
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ float ld_float(const T *p);
+template <>
+__device__ __forceinline__ float ld_float<__half>(const __half *p) { return __half2float(*p); }
+template <>
+__device__ __forceinline__ float ld_float<__nv_bfloat16>(const __nv_bfloat16 *p) {
+  return __bfloat162float(*p);
+}
+
+// Geometry of (tile row r, tap t): base element offset of corner (h_low, w_low)
+// and the four corner weights (mask folded in, 0 for dropped corners).
+template <typename T>
+__device__ __forceinline__ void tap_geometry(const TcParams &p, const T *__restrict__ off,
+                                             const T *__restrict__ msk, int m, int t, int &base,
+                                             uint4 &wq) {
+  base = 0;
+  wq = make_uint4(0u, 0u, 0u, 0u);
+  if (m >= p.M) return;
+  const int HoWo = p.Ho * p.Wo;
+  const int b = m / HoWo;
+  const int rem = m - b * HoWo;
+  const int oh = rem / p.Wo;
+  const int ow = rem - oh * p.Wo;
+  const int ki = t / p.kW, kj = t - (t / p.kW) * p.kW;
+  const T *ob = off + b * p.os[0] + oh * p.os[2] + ow * p.os[3];
+  const float off_h = ld_float(ob + (2 * t) * p.os[1]);
+  const float off_w = ld_float(ob + (2 * t + 1) * p.os[1]);
+  float mk = ld_float(msk + b * p.ms[0] + t * p.ms[1] + oh * p.ms[2] + ow * p.ms[3]);
+  if (p.mask_is_logit) mk = 1.f / (1.f + __expf(-mk));
+  const float h_im = static_cast<float>(oh * p.sh - p.ph + ki * p.dh) + off_h;
+  const float w_im = static_cast<float>(ow * p.sw - p.pw + kj * p.dw) + off_w;
+  if (!(h_im > -1.f && w_im > -1.f && h_im < static_cast<float>(p.H) &&
+        w_im < static_cast<float>(p.W)))
+    return;
+  const int h_low = static_cast<int>(floorf(h_im));
+  const int w_low = static_cast<int>(floorf(w_im));
+  const float lh = h_im - static_cast<float>(h_low), lw = w_im - static_cast<float>(w_low);
+  const float hh = 1.f - lh, hw = 1.f - lw;
+  const bool y0 = h_low >= 0, y1 = h_low + 1 <= p.H - 1;
+  const bool x0 = w_low >= 0, x1 = w_low + 1 <= p.W - 1;
+  base = b * p.xs0 + h_low * p.xs2 + w_low * p.xs3;
+  wq.x = (y0 && x0) ? GatherMath<T>::pack_weight(hh * hw * mk) : 0u;
+  wq.y = (y0 && x1) ? GatherMath<T>::pack_weight(hh * lw * mk) : 0u;
+  wq.z = (y1 && x0) ? GatherMath<T>::pack_weight(lh * hw * mk) : 0u;
+  wq.w = (y1 && x1) ? GatherMath<T>::pack_weight(lh * lw * mk) : 0u;
+}
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
+                  const T *__restrict__ x, const T *__restrict__ off, const T *__restrict__ msk,
+                  const T *__restrict__ bias, T *__restrict__ y) {
+  using L = Smem<BN, STAGES>;
+  using GM = GatherMath<T>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = ptx::smem_u32(smem);
+  const uint32_t sA = sbase + L::kA, sB = sbase + L::kB;
+  uint4 *s_gw = reinterpret_cast<uint4 *>(smem + L::kGW);
+  int *s_gb = reinterpret_cast<int *>(smem + L::kGB);
+  const uint32_t bar_full = sbase + L::kBar;            // A stage written (gather warps)
+  const uint32_t bar_wfull = bar_full + STAGES * 8;     // B stage landed (TMA bytes)
+  const uint32_t bar_empty = bar_wfull + STAGES * 8;    // stage consumed (tcgen05.commit)
+  const uint32_t bar_tmem = bar_empty + STAGES * 8;
+  uint32_t *s_tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kMisc);
+  volatile int *s_abort = reinterpret_cast<volatile int *>(smem + L::kMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tile = blockIdx.x;
+  const int n_tile = tile % p.n_tiles_n;
+  const int m0 = (tile / p.n_tiles_n) * kBM;
+  const int n0 = n_tile * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(bar_full + 8 * s, kGatherWarps);      // one arrive per gather warp
+      ptx::mbar_init(bar_wfull + 8 * s, 1);                // TMA arrive + transaction bytes
+      ptx::mbar_init(bar_empty + 8 * s, 1);                // tcgen05.commit
+    }
+    ptx::mbar_init(bar_tmem, 1);
+    *s_abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    ptx::tmem_alloc(ptx::smem_u32(s_tmem_slot), BN);
+    ptx::tmem_relinquish();
+  }
+  if (warp == kTmaWarp && lane == 0) ptx::tma_prefetch_desc(&tmap_w);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *s_tmem_slot;
+
+  if (warp < kGatherWarps) {
+    // ---------------------------------------------------------- geometry
+    for (int e = threadIdx.x; e < p.T * kBM; e += kGatherWarps * 32) {
+      const int t = e / kBM, r = e - (e / kBM) * kBM;
+      int base;
+      uint4 wq;
+      tap_geometry<T>(p, off, msk, m0 + r, t, base, wq);
+      s_gb[e] = base;
+      s_gw[e] = wq;
+    }
+    ptx::named_barrier_sync(1, kGatherWarps * 32);
+
+    // ---------------------------------------------------------- gather
+    const int j = lane & 7;     // 16-byte chunk (8 channels) within the 128-byte row
+    const int rsub = lane >> 3; // row within the warp's group of 4
+    const int xs2 = p.xs2, xs3 = p.xs3;
+    bool ok = true;
+    for (int kit = 0; kit < p.n_k && ok; ++kit) {
+      const int s = kit % STAGES;
+      const uint32_t ph = (kit / STAGES) & 1;
+      ok = ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1, s_abort, &g_bevk_watchdog,
+                                  kSiteGatherEmpty);
+      if (!ok) break;
+      const int t = p.tap_major ? kit / p.n_cc : kit % p.T;
+      const int cc = p.tap_major ? kit - (kit / p.n_cc) * p.n_cc : kit / p.T;
+      const int c = cc * kBK + j * 8;
+      const bool cvalid = c < p.Cin;
+      const uint32_t a_stage = sA + s * L::kABytes;
+#pragma unroll
+      for (int i = 0; i < kBM / (kGatherWarps * 4); ++i) {
+        const int r = i * (kGatherWarps * 4) + warp * 4 + rsub;
+        const int e = t * kBM + r;
+        const uint4 wq = s_gw[e];
+        uint4 res = make_uint4(0u, 0u, 0u, 0u);
+        if (cvalid) {
+          const T *px = x + static_cast<int64_t>(s_gb[e]) + c;
+          uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0, v2 = v0, v3 = v0;
+          if (wq.x) v0 = __ldg(reinterpret_cast<const uint4 *>(px));
+          if (wq.y) v1 = __ldg(reinterpret_cast<const uint4 *>(px + xs3));
+          if (wq.z) v2 = __ldg(reinterpret_cast<const uint4 *>(px + xs2));
+          if (wq.w) v3 = __ldg(reinterpret_cast<const uint4 *>(px + xs2 + xs3));
+          res.x = GM::lerp2(wq, v0.x, v1.x, v2.x, v3.x);
+          res.y = GM::lerp2(wq, v0.y, v1.y, v2.y, v3.y);
+          res.z = GM::lerp2(wq, v0.z, v1.z, v2.z, v3.z);
+          res.w = GM::lerp2(wq, v0.w, v1.w, v2.w, v3.w);
+        }
+        ptx::st_shared_v4(a_stage + r * 128 + ((j ^ (r & 7)) << 4), res);
+      }
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_full + 8 * s);
+    }
+
+    // ---------------------------------------------------------- epilogue
+    if (ok) ok = ptx::mbar_wait_bounded(bar_tmem, 0, s_abort, &g_bevk_watchdog, kSiteEpilogue);
+    if (ok) {
+      ptx::tc_fence_after();
+      const int q = warp & 3;          // TMEM lane quadrant of this warp
+      const int half = warp >> 2;      // which half of the BN columns
+      const int row = q * 32 + lane;
+      const int m = m0 + row;
+      const int HoWo = p.Ho * p.Wo;
+      const int b = m / HoWo, rem = m - (m / HoWo) * HoWo;
+      const int oh = rem / p.Wo, ow = rem - (rem / p.Wo) * p.Wo;
+      T *yrow = y + b * p.ys[0] + oh * p.ys[2] + ow * p.ys[3];
+      const bool vec_out = p.ys[1] == 1 && (p.Cout & 7) == 0 &&
+                           (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (p.ys[0] & 7) == 0 &&
+                           (p.ys[2] & 7) == 0 && (p.ys[3] & 7) == 0;
+#pragma unroll 1
+      for (int cb = 0; cb < BN / 2; cb += 32) {
+        const int col = half * (BN / 2) + cb;
+        if (n0 + col >= p.Cout) break;
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + col, r);
+        ptx::tmem_wait_ld();
+        if (m < p.M) {
+          const int co0 = n0 + col;
+          float v[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            v[jj] = __uint_as_float(r[jj]);
+            if (p.has_bias && co0 + jj < p.Cout) v[jj] += ld_float(bias + co0 + jj);
+          }
+          if (vec_out && co0 + 32 <= p.Cout) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint4 pk;
+              uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
+#pragma unroll
+              for (int h = 0; h < 4; ++h)
+                pw[h] = static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h])) |
+                        (static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h + 1])) << 16);
+              *reinterpret_cast<uint4 *>(yrow + co0 + g * 8) = pk;
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+              if (co0 + jj < p.Cout) {
+                const uint16_t bits = GM::store_bits(v[jj]);
+                *reinterpret_cast<uint16_t *>(yrow + (co0 + jj) * p.ys[1]) = bits;
+              }
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == kTmaWarp) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kit = 0; kit < p.n_k; ++kit) {
+        const int s = kit % STAGES;
+        const uint32_t ph = (kit / STAGES) & 1;
+        if (!ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1, s_abort, &g_bevk_watchdog,
+                                    kSiteTmaEmpty))
+          break;
+        const int t = p.tap_major ? kit / p.n_cc : kit % p.T;
+        const int cc = p.tap_major ? kit - (kit / p.n_cc) * p.n_cc : kit / p.T;
+        ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, L::kBBytes);
+        ptx::tma_load_2d(sB + s * L::kBBytes, &tmap_w, bar_wfull + 8 * s, t * p.Cin_pad + cc * kBK,
+                         n0);
+        issued = kit + 1;
+      }
+      if (*s_abort) {
+        // Let this CTA's own copies land before its shared memory is released.
+        volatile int never = 0;
+        for (int kit = issued - STAGES < 0 ? 0 : issued - STAGES; kit < issued; ++kit)
+          ptx::mbar_wait_bounded(bar_wfull + 8 * (kit % STAGES), (kit / STAGES) & 1, &never,
+                                 &g_bevk_watchdog, kSiteTmaEmpty);
+      }
+    }
+  } else {  // MMA warp
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::umma_idesc_f16(GM::kFmt, kBM, BN);
+      for (int kit = 0; kit < p.n_k; ++kit) {
+        const int s = kit % STAGES;
+        const uint32_t ph = (kit / STAGES) & 1;
+        if (!ptx::mbar_wait_bounded(bar_wfull + 8 * s, ph, s_abort, &g_bevk_watchdog,
+                                    kSiteMmaFull) ||
+            !ptx::mbar_wait_bounded(bar_full + 8 * s, ph, s_abort, &g_bevk_watchdog,
+                                    kSiteMmaFull))
+          break;
+        ptx::tc_fence_after();
+        const uint32_t a_stage = sA + s * L::kABytes;
+        const uint32_t b_stage = sB + s * L::kBBytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          ptx::umma_f16_ss(tmem_base, ptx::umma_desc_sw128(a_stage + k * 32),
+                           ptx::umma_desc_sw128(b_stage + k * 32), idesc,
+                           (kit | k) != 0 ? 1u : 0u);
+        }
+        ptx::umma_commit(bar_empty + 8 * s);
+      }
+      // Tracks completion of every MMA issued above (also on abort, so the
+      // accumulator is quiescent before TMEM is released).
+      ptx::umma_commit(bar_tmem);
+      if (*s_abort) {
+        volatile int dummy = 0;
+        ptx::mbar_wait_bounded(bar_tmem, 0, &dummy, &g_bevk_watchdog, kSiteEpilogue);
+      }
+    }
+    __syncwarp();
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, BN);
+  }
+}
+
+// ---------------------------------------------------------------- host
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+template <typename T, int BN, int STAGES>
+int launch_tc(const TcParams &p, const CUtensorMap &tmap, const void *x, const void *off,
+              const void *msk, const void *bias, void *y, int tiles, cudaStream_t stream) {
+  using L = Smem<BN, STAGES>;
+  static_assert(L::kAlloc <= 232448, "shared memory budget");
+  auto kern = dcn_fwd_tc_kernel<T, BN, STAGES>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+  });
+  if (attr_err != cudaSuccess)
+    return fail(BEVK_ERR_CUDA, "dcn tc: cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+  kern<<<tiles, kThreads, L::kAlloc, stream>>>(tmap, p, static_cast<const T *>(x),
+                                               static_cast<const T *>(off),
+                                               static_cast<const T *>(msk),
+                                               static_cast<const T *>(bias), static_cast<T *>(y));
+  return check_launch("dcn_fwd_tc_kernel");
+}
+
+}  // namespace
+
+bool dcn_tc_supported(const bevk_dcn_problem *pr, const DcnDims &d) {
+  if (pr->dtype != BEVK_DTYPE_F16 && pr->dtype != BEVK_DTYPE_BF16) return false;
+  if (d.groups != 1 || d.dg != 1) return false;
+  if (d.Cin % 8 != 0 || d.T > kMaxTaps) return false;
+  if (d.M >= (int64_t(1) << 31) - kBM) return false;
+  const int dev = current_device();
+  if (dev < 0 || device_info(dev).cc_major != 10) return false;
+  return true;
+}
+
+int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const void *x,
+                          const int64_t xs[4], const void *off, const void *msk,
+                          const void *wpk, const void *bias, void *y, cudaStream_t stream) {
+  if (xs[1] != 1 || xs[0] % 8 || xs[2] % 8 || xs[3] % 8 || !aligned(x, 16) || !aligned(wpk, 16))
+    return fail(BEVK_ERR_MISALIGNED, "dcn tc: input must be channel-contiguous with 16-byte rows");
+  // int32 element offsets inside the kernel
+  const int64_t extent = (d.B - 1) * xs[0] + (d.H - 1) * xs[2] + (d.W - 1) * xs[3] + d.Cin;
+  if (extent >= (int64_t(1) << 31) || xs[0] >= (int64_t(1) << 31))
+    return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn tc: input extent exceeds 32-bit indexing");
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(BEVK_ERR_CUDA, "dcn tc: cuTensorMapEncodeTiled unavailable");
+
+  const int BN = d.Cout <= 64 ? 64 : (d.Cout <= 128 ? 128 : 256);
+  TcParams p;
+  p.Cin = d.Cin; p.H = d.H; p.W = d.W; p.Ho = d.Ho; p.Wo = d.Wo; p.Cout = d.Cout;
+  p.kW = d.kW; p.T = d.T;
+  p.sh = d.sh; p.sw = d.sw; p.ph = d.ph; p.pw = d.pw; p.dh = d.dh; p.dw = d.dw;
+  p.M = static_cast<int>(d.M);
+  p.Cin_pad = d.Cin_g_pad;
+  p.n_cc = p.Cin_pad / kBK;
+  p.n_k = p.T * p.n_cc;
+  p.n_tiles_n = (d.Cout + BN - 1) / BN;
+  p.tap_major = 0;
+  p.mask_is_logit = pr->mask_is_logit;
+  p.has_bias = pr->has_bias;
+  p.xs0 = static_cast<int>(xs[0]); p.xs2 = static_cast<int>(xs[2]); p.xs3 = static_cast<int>(xs[3]);
+  for (int i = 0; i < 4; ++i) {
+    p.os[i] = pr->offset_strides[i];
+    p.ms[i] = pr->mask_strides[i];
+    p.ys[i] = pr->output_strides[i];
+  }
+  const int64_t tiles = ((d.M + kBM - 1) / kBM) * p.n_tiles_n;
+  if (tiles > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn tc: too many tiles");
+
+  CUtensorMap tmap;
+  const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(d.T) * p.Cin_pad,
+                              static_cast<cuuint64_t>(d.Cout)};
+  const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(d.T) * p.Cin_pad * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(BN)};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUtensorMapDataType dt = pr->dtype == BEVK_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUresult cr = enc(&tmap, dt, 2, const_cast<void *>(wpk), gdim, gstride, box, estride,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(BEVK_ERR_CUDA, "dcn tc: tensor map encode failed (%d)", int(cr));
+
+  const int nt = static_cast<int>(tiles);
+  if (pr->dtype == BEVK_DTYPE_F16) {
+    if (BN == 256) return launch_tc<__half, 256, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
+    if (BN == 128) return launch_tc<__half, 128, 6>(p, tmap, x, off, msk, bias, y, nt, stream);
+    return launch_tc<__half, 64, 8>(p, tmap, x, off, msk, bias, y, nt, stream);
+  }
+  if (BN == 256) return launch_tc<__nv_bfloat16, 256, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
+  if (BN == 128) return launch_tc<__nv_bfloat16, 128, 6>(p, tmap, x, off, msk, bias, y, nt, stream);
+  return launch_tc<__nv_bfloat16, 64, 8>(p, tmap, x, off, msk, bias, y, nt, stream);
+}
+
+int read_and_clear_watchdog(int device, unsigned int *code) {
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (cudaSetDevice(device) != cudaSuccess) return fail(BEVK_ERR_INVALID_ARGUMENT, "watchdog: bad device %d", device);
+  unsigned int v = 0, zero = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_bevk_watchdog, sizeof(v));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_bevk_watchdog, &zero, sizeof(zero));
+  if (prev >= 0) cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(BEVK_ERR_CUDA, "watchdog: %s", cudaGetErrorString(e));
+  if (code) *code = v;
+  return v ? fail(BEVK_ERR_DEVICE_TIMEOUT, "device watchdog fired at site 0x%x", v) : BEVK_OK;
+}
+
+}  // namespace bevk

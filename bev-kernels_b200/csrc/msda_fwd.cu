@@ -1,0 +1,270 @@
+// msda_fwd.cu -- multi-scale deformable attention forward for sm_100a.
+//
+// Semantics follow csrc_musa/msda/ms_deform_attn_kernels.cuh:559-623 (generic
+// im2col) and :51-284 (spec warp kernel):
+//   out[b, q, m*C + c] = sum_{l,p} attn[b,q,m,l,p] * bilinear(value_l[b, :, m, c],
+//                        h = loc_y*H_l - 0.5, w = loc_x*W_l - 0.5)
+// with a sample dropped unless -1 < h < H_l and -1 < w < W_l and each of the
+// four corners zeroed outside [0, H_l-1] x [0, W_l-1].
+//
+// Design (C == 32, the BEVFormer head dim): one warp owns one (b, q, head)
+// unit.  Phase 1: lane s computes the geometry of sample s (up to 32 samples
+// per pass) -- level, corner indices, and the four corner weights with the
+// attention weight folded in -- and parks it in shared memory.  Phase 2: for
+// each sample the warp issues ONE load covering all four corners: lanes
+// 8g..8g+7 read corner g's 32-channel line (128 B for fp32) as 4-channel
+// vectors, so every load instruction moves four full lines.  Each lane keeps
+// a 4-channel partial sum for its corner slot; the four slots are folded with
+// two shuffles at the end.  No tensor cores: this is a gather, not a
+// contraction.  Any other C falls back to one thread per output element.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "bevk_internal.h"
+
+namespace bevk {
+namespace {
+
+constexpr int kMaxLevels = 16;
+
+template <typename T>
+struct Vec4;  // 4 channels of T, loaded as one vector
+template <>
+struct Vec4<float> {
+  using type = float4;
+  __device__ static float4 to_f32(float4 v) { return v; }
+  __device__ static float4 from_f32(float4 v) { return v; }
+};
+template <>
+struct Vec4<__half> {
+  using type = uint2;
+  __device__ static float4 to_f32(uint2 v) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  __device__ static uint2 from_f32(float4 f) {
+    __half2 a = __floats2half2_rn(f.x, f.y), b = __floats2half2_rn(f.z, f.w);
+    return make_uint2(*reinterpret_cast<uint32_t *>(&a), *reinterpret_cast<uint32_t *>(&b));
+  }
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+  using type = uint2;
+  __device__ static float4 to_f32(uint2 v) {
+    return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u),
+                       __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xFFFF0000u));
+  }
+  __device__ static uint2 from_f32(float4 f) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(f.x, f.y), b = __floats2bfloat162_rn(f.z, f.w);
+    return make_uint2(*reinterpret_cast<uint32_t *>(&a), *reinterpret_cast<uint32_t *>(&b));
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v) { return static_cast<float>(v); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v) { return static_cast<T>(v); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Geometry of one sample for the four corner slots: line index (pixel*heads +
+// head, relative to the batch's value base) and weight (bilinear * attn; 0 for
+// a dropped corner).
+struct SampleGeom {
+  int idx[4];
+  float w[4];
+};
+
+constexpr int kWarps = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32)
+msda_fwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ shapes,
+                    const int64_t *__restrict__ lsi, const T *__restrict__ loc,
+                    const T *__restrict__ attn, T *__restrict__ out, int S, int heads,
+                    int L, int Q, int P, int64_t units) {
+  using V = Vec4<T>;
+  using VT = typename V::type;
+  constexpr int C = 32;
+  __shared__ int s_lvl[kMaxLevels][3];  // H, W, start
+  __shared__ SampleGeom s_geom[kWarps][32];
+
+  if (threadIdx.x < L) {
+    s_lvl[threadIdx.x][0] = static_cast<int>(shapes[2 * threadIdx.x]);
+    s_lvl[threadIdx.x][1] = static_cast<int>(shapes[2 * threadIdx.x + 1]);
+    s_lvl[threadIdx.x][2] = static_cast<int>(lsi[threadIdx.x]);
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t unit = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  if (unit >= units) return;
+
+  const int m = static_cast<int>(unit % heads);
+  const int64_t b = unit / (static_cast<int64_t>(Q) * heads);
+  const VT *vbase = reinterpret_cast<const VT *>(value + b * S * heads * C);
+  const int LP = L * P;
+  const T *uloc = loc + unit * LP * 2;
+  const T *uattn = attn + unit * LP;
+
+  const int g = lane >> 3;  // corner slot
+  const int j = lane & 7;   // 4-channel vector within the head's 32 channels
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  for (int s0 = 0; s0 < LP; s0 += 32) {
+    const int s = s0 + lane;
+    SampleGeom geo;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { geo.idx[k] = 0; geo.w[k] = 0.f; }
+    if (s < LP) {
+      const int l = s / P;
+      const int Hl = s_lvl[l][0], Wl = s_lvl[l][1], start = s_lvl[l][2];
+      const float lx = to_f32(uloc[2 * s]);
+      const float ly = to_f32(uloc[2 * s + 1]);
+      const float a = to_f32(uattn[s]);
+      const float h_im = ly * static_cast<float>(Hl) - 0.5f;
+      const float w_im = lx * static_cast<float>(Wl) - 0.5f;
+      if (h_im > -1.f && w_im > -1.f && h_im < static_cast<float>(Hl) &&
+          w_im < static_cast<float>(Wl)) {
+        const int h_low = static_cast<int>(floorf(h_im));
+        const int w_low = static_cast<int>(floorf(w_im));
+        const float lh = h_im - static_cast<float>(h_low);
+        const float lw = w_im - static_cast<float>(w_low);
+        const float hh = 1.f - lh, hw = 1.f - lw;
+        const bool y0 = h_low >= 0, y1 = h_low + 1 <= Hl - 1;
+        const bool x0 = w_low >= 0, x1 = w_low + 1 <= Wl - 1;
+        const int base = start + h_low * Wl + w_low;  // pixel of corner (y0, x0)
+        if (y0 && x0) { geo.idx[0] = base * heads + m;            geo.w[0] = hh * hw * a; }
+        if (y0 && x1) { geo.idx[1] = (base + 1) * heads + m;      geo.w[1] = hh * lw * a; }
+        if (y1 && x0) { geo.idx[2] = (base + Wl) * heads + m;     geo.w[2] = lh * hw * a; }
+        if (y1 && x1) { geo.idx[3] = (base + Wl + 1) * heads + m; geo.w[3] = lh * lw * a; }
+      }
+    }
+    s_geom[warp][lane] = geo;
+    __syncwarp();
+    const int n = min(32, LP - s0);
+#pragma unroll 8
+    for (int i = 0; i < n; ++i) {
+      const int idx = s_geom[warp][i].idx[g];
+      const float w = s_geom[warp][i].w[g];
+      if (w != 0.f) {
+        const float4 v = V::to_f32(__ldg(vbase + static_cast<int64_t>(idx) * (C / 4) + j));
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+      }
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int o = 8; o <= 16; o <<= 1) {
+    acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+    acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+    acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+    acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+  }
+  if (lane < 8) reinterpret_cast<VT *>(out + unit * C)[j] = V::from_f32(acc);
+}
+
+// Any head dim: one thread per output element (b, q, m, c).
+template <typename T>
+__global__ void __launch_bounds__(256)
+msda_fwd_generic_kernel(const T *__restrict__ value, const int64_t *__restrict__ shapes,
+                        const int64_t *__restrict__ lsi, const T *__restrict__ loc,
+                        const T *__restrict__ attn, T *__restrict__ out, int S, int heads,
+                        int C, int L, int Q, int P, int64_t n) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int c = static_cast<int>(i % C);
+  const int64_t unit = i / C;
+  const int m = static_cast<int>(unit % heads);
+  const int64_t b = unit / (static_cast<int64_t>(Q) * heads);
+  const int LP = L * P;
+  const T *uloc = loc + unit * LP * 2;
+  const T *uattn = attn + unit * LP;
+  float acc = 0.f;
+  for (int l = 0; l < L; ++l) {
+    const int Hl = static_cast<int>(shapes[2 * l]), Wl = static_cast<int>(shapes[2 * l + 1]);
+    const T *vl = value + (b * S + lsi[l]) * heads * C + static_cast<int64_t>(m) * C + c;
+    const int64_t ws = static_cast<int64_t>(heads) * C, hs = Wl * ws;
+    for (int p = 0; p < P; ++p) {
+      const int s = l * P + p;
+      const float h_im = to_f32(uloc[2 * s + 1]) * static_cast<float>(Hl) - 0.5f;
+      const float w_im = to_f32(uloc[2 * s]) * static_cast<float>(Wl) - 0.5f;
+      if (!(h_im > -1.f && w_im > -1.f && h_im < static_cast<float>(Hl) &&
+            w_im < static_cast<float>(Wl)))
+        continue;
+      const int h_low = static_cast<int>(floorf(h_im)), w_low = static_cast<int>(floorf(w_im));
+      const float lh = h_im - h_low, lw = w_im - w_low, hh = 1.f - lh, hw = 1.f - lw;
+      float v1 = 0.f, v2 = 0.f, v3 = 0.f, v4 = 0.f;
+      if (h_low >= 0 && w_low >= 0) v1 = to_f32(vl[h_low * hs + w_low * ws]);
+      if (h_low >= 0 && w_low + 1 <= Wl - 1) v2 = to_f32(vl[h_low * hs + (w_low + 1) * ws]);
+      if (h_low + 1 <= Hl - 1 && w_low >= 0) v3 = to_f32(vl[(h_low + 1) * hs + w_low * ws]);
+      if (h_low + 1 <= Hl - 1 && w_low + 1 <= Wl - 1)
+        v4 = to_f32(vl[(h_low + 1) * hs + (w_low + 1) * ws]);
+      acc += (hh * hw * v1 + hh * lw * v2 + lh * hw * v3 + lh * lw * v4) * to_f32(uattn[s]);
+    }
+  }
+  out[i] = from_f32<T>(acc);
+}
+
+template <typename T>
+int launch_typed(const void *value, const int64_t *shapes, const int64_t *lsi, const void *loc,
+                 const void *attn, int B, int S, int heads, int C, int L, int Q, int P,
+                 void *out, cudaStream_t stream) {
+  const int64_t units = static_cast<int64_t>(B) * Q * heads;
+  if (units == 0) return BEVK_OK;
+  const size_t vec_bytes = sizeof(T) * 4;
+  const bool fast = C == 32 && L <= kMaxLevels && aligned(value, vec_bytes) &&
+                    aligned(out, vec_bytes);
+  if (fast) {
+    const int64_t blocks = (units + kWarps - 1) / kWarps;
+    if (blocks > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "msda: grid too large");
+    msda_fwd_c32_kernel<T><<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(
+        static_cast<const T *>(value), shapes, lsi, static_cast<const T *>(loc),
+        static_cast<const T *>(attn), static_cast<T *>(out), S, heads, L, Q, P, units);
+    return check_launch("msda_fwd_c32_kernel");
+  }
+  const int64_t n = units * C;
+  const int64_t blocks = (n + 255) / 256;
+  if (blocks > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "msda: grid too large");
+  msda_fwd_generic_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      static_cast<const T *>(value), shapes, lsi, static_cast<const T *>(loc),
+      static_cast<const T *>(attn), static_cast<T *>(out), S, heads, C, L, Q, P, n);
+  return check_launch("msda_fwd_generic_kernel");
+}
+
+}  // namespace
+
+int launch_msda_forward(const void *value, const int64_t *shapes, const int64_t *lsi,
+                        const void *loc, const void *attn, int B, int S, int heads, int C,
+                        int L, int Q, int P, void *out, int dtype, cudaStream_t stream) {
+  switch (dtype) {
+    case BEVK_DTYPE_F32:
+      return launch_typed<float>(value, shapes, lsi, loc, attn, B, S, heads, C, L, Q, P, out,
+                                 stream);
+    case BEVK_DTYPE_F16:
+      return launch_typed<__half>(value, shapes, lsi, loc, attn, B, S, heads, C, L, Q, P, out,
+                                  stream);
+    case BEVK_DTYPE_BF16:
+      return launch_typed<__nv_bfloat16>(value, shapes, lsi, loc, attn, B, S, heads, C, L, Q, P,
+                                         out, stream);
+    default:
+      return fail(BEVK_ERR_UNSUPPORTED, "msda: dtype %d not supported (f32, f16, bf16)", dtype);
+  }
+}
+
+}  // namespace bevk

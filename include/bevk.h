@@ -1,0 +1,209 @@
+/*
+ * bevk.h -- C ABI of the B200 (sm_100a) deformable-sampling kernels.
+ *
+ * Plain pointers, sizes and strides; no torch types.  Every entry point
+ *   - takes device pointers that it borrows for the duration of the call,
+ *   - never allocates or frees device memory (scratch comes from the caller
+ *     through an explicit workspace argument),
+ *   - enqueues its kernels asynchronously on the given stream (NULL = the
+ *     legacy default stream) of the current CUDA device,
+ *   - returns BEVK_OK or a negative status; bevk_last_error_message() then
+ *     holds a human-readable reason for the calling thread.
+ *
+ * Shapes follow the reference operator surface (naotic/bev-kernels):
+ *   DCNv2:  input [B, Cin, H, W], offset [B, 2*dg*kH*kW, Ho, Wo] with channel
+ *           2t = dh and 2t+1 = dw of tap t = ki*kW + kj, mask [B, dg*kH*kW, Ho, Wo],
+ *           weight [Cout, Cin/groups, kH, kW], output [B, Cout, Ho, Wo].
+ *           Any of them may be channels-last; strides describe the layout.
+ *   MSDA:   value [B, S, heads, C], spatial_shapes [L, 2] int64 (H, W),
+ *           level_start_index [L] int64, sampling_loc [B, Q, heads, L, P, 2]
+ *           (x then y, normalised to [0, 1]), attention_weights [B, Q, heads, L, P],
+ *           output [B, Q, heads*C].
+ */
+#ifndef BEVK_H_
+#define BEVK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define BEVK_API
+#else
+#define BEVK_API __attribute__((visibility("default")))
+#endif
+
+/* Same underlying type as cudaStream_t / CUstream. */
+typedef struct CUstream_st *bevk_stream_t;
+
+/* Element types. */
+enum bevk_dtype {
+  BEVK_DTYPE_F32 = 0,
+  BEVK_DTYPE_F16 = 1,
+  BEVK_DTYPE_BF16 = 2,
+  BEVK_DTYPE_F64 = 3
+};
+
+/* Status codes (0 = success). */
+enum bevk_status {
+  BEVK_OK = 0,
+  BEVK_ERR_INVALID_ARGUMENT = -1, /* null pointer, bad shape, bad stride     */
+  BEVK_ERR_UNSUPPORTED = -2,      /* dtype / geometry this build cannot run */
+  BEVK_ERR_INDEX_OVERFLOW = -3,   /* tensor too large for 32-bit indexing   */
+  BEVK_ERR_MISALIGNED = -4,       /* pointer/stride alignment requirement   */
+  BEVK_ERR_CUDA = -5,             /* CUDA runtime / launch failure          */
+  BEVK_ERR_WORKSPACE = -6,        /* workspace missing or too small         */
+  BEVK_ERR_DEVICE_TIMEOUT = -7    /* a kernel's bounded wait gave up        */
+};
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+BEVK_API int bevk_version(void);
+/* Static description of a status code. */
+BEVK_API const char *bevk_status_string(int status);
+/* Detail of the most recent failure on the calling thread ("" if none). */
+BEVK_API const char *bevk_last_error_message(void);
+
+/*
+ * Device-side watchdog.  Kernels that wait on barriers bound every wait; a
+ * wait that gives up records a nonzero code in a per-device word instead of
+ * hanging.  This call synchronises the given device, returns the word in
+ * *code (0 = clean) and clears it.  Returns BEVK_ERR_DEVICE_TIMEOUT when the
+ * word was set, BEVK_OK otherwise.
+ */
+BEVK_API int bevk_device_watchdog(int device, unsigned int *code);
+
+/* ------------------------------------------------------------------------ */
+/* DCNv2 (modulated deformable convolution), forward                        */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Problem description shared by the DCN entry points.  Strides are element
+ * strides in (b, c, h, w) order for each 4-D tensor; output spatial size is
+ * derived as (in + 2*pad - (dil*(k-1)+1)) / stride + 1.
+ */
+typedef struct bevk_dcn_problem {
+  int dtype;                 /* enum bevk_dtype; all tensors share it        */
+  int batch, in_channels, height, width;
+  int out_channels, kernel_h, kernel_w;
+  int stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w;
+  int groups, deformable_groups;
+  int64_t input_strides[4];
+  int64_t offset_strides[4];
+  int64_t mask_strides[4];
+  int64_t output_strides[4];
+  int mask_is_logit;         /* 1: mask holds pre-sigmoid values; sigmoid is
+                                applied on load (the fused offset-conv output
+                                path of dcn_split_nhwc.py:159-174)             */
+  int has_bias;
+} bevk_dcn_problem;
+
+/* Output height/width of a problem (BEVK_ERR_INVALID_ARGUMENT if <= 0). */
+BEVK_API int bevk_dcn_output_size(const bevk_dcn_problem *p, int *height_out,
+                                  int *width_out);
+
+/*
+ * Packed weight layout used by bevk_dcn_forward: [Cout][kH*kW][Cin_g_pad] in
+ * the problem dtype, Cin_g = Cin/groups rounded up to a multiple of 64 with
+ * zeros, so every output channel's reduction row is tap-major and contiguous.
+ * Packing is a one-off per weight update (the reference re-packs on every
+ * call: dcn_split_nhwc.py:176).
+ */
+BEVK_API size_t bevk_dcn_packed_weight_bytes(const bevk_dcn_problem *p);
+/* weight: [Cout, Cin/groups, kH, kW] contiguous. */
+BEVK_API int bevk_dcn_pack_weight(const bevk_dcn_problem *p, const void *weight,
+                                  void *packed_weight, bevk_stream_t stream);
+
+/* Scratch bytes bevk_dcn_forward needs for this problem (0 when none). */
+BEVK_API size_t bevk_dcn_forward_workspace_bytes(const bevk_dcn_problem *p);
+
+/*
+ * Fused DCNv2 forward: output = conv(weight, deformable-bilinear(input,
+ * offset) * mask) + bias, without materialising the column matrix.
+ *
+ * Replaces ModulatedDeformConv2dFunction.forward
+ * (modulated_deform_conv/modulated_deform_conv.py:331-403: im2col_opt + torch.mm
+ * + permute + bias) and the gather + GEMM of DCNSplitNHWCFunction.forward
+ * (modulated_deform_conv/dcn_split_nhwc.py:159-203).
+ *
+ * fp16/bf16 with groups == 1, deformable_groups == 1, Cin % 8 == 0 and
+ * kH*kW <= 9 run the tcgen05 tensor-core kernel (fp32 accumulation in TMEM);
+ * every other case (fp32, fp64, grouped, ...) runs the exact SIMT kernel.
+ * bias may be NULL when has_bias == 0.
+ */
+BEVK_API int bevk_dcn_forward(const bevk_dcn_problem *p, const void *input,
+                              const void *offset, const void *mask,
+                              const void *packed_weight, const void *bias,
+                              void *output, void *workspace,
+                              size_t workspace_bytes, bevk_stream_t stream);
+
+/*
+ * Column-matrix ops of the reference extension (binding names kept).
+ *
+ * bevk_modulated_deformable_im2col / _opt replace
+ *   modulated_deformable_im2col_cuda      (csrc/binding.cpp:5-11, :143-145)
+ *   modulated_deformable_im2col_opt_cuda  (csrc/binding.cpp:21-27, :149-151)
+ * NCHW contiguous input/offset/mask; data_col is the [C*kH*kW, B*Ho*Wo] matrix
+ * (row c*kH*kW + t).  Every element is written.
+ */
+BEVK_API int bevk_modulated_deformable_im2col(
+    const void *data_im, const void *data_offset, const void *data_mask,
+    int batch_size, int channels, int height_im, int width_im, int height_col,
+    int width_col, int kernel_h, int kernel_w, int pad_h, int pad_w,
+    int stride_h, int stride_w, int dilation_h, int dilation_w,
+    int deformable_group, void *data_col, int dtype, bevk_stream_t stream);
+
+BEVK_API int bevk_modulated_deformable_im2col_opt(
+    const void *data_im, const void *data_offset, const void *data_mask,
+    int batch_size, int channels, int height_im, int width_im, int height_col,
+    int width_col, int kernel_h, int kernel_w, int pad_h, int pad_w,
+    int stride_h, int stride_w, int dilation_h, int dilation_w,
+    int deformable_group, void *data_col, int dtype, bevk_stream_t stream);
+
+/*
+ * replaces modulated_deformable_im2col_nhwc_cuda (csrc/binding.cpp:61-67,
+ * :163-165; launcher csrc/dcn_fused_nhwc_cuda.cu:27-87).
+ * data_im [B, H, W, C]; data_offset [B, Ho, Wo, offset_last_dim] where
+ * offset_last_dim is 2*kH*kW (offset only; data_mask is [B, Ho, Wo, kH*kW]
+ * post-sigmoid) or 3*kH*kW (the raw offset-conv output y: offsets in
+ * [0, 2T), pre-sigmoid mask in [2T, 3T); data_mask is ignored).
+ * data_col is [B*Ho*Wo, kH*kW*C] with k = t*C + c.  deformable_group must
+ * be 1 (as in the reference).
+ */
+BEVK_API int bevk_modulated_deformable_im2col_nhwc(
+    const void *data_im, const void *data_offset, const void *data_mask,
+    int batch_size, int channels, int height_im, int width_im, int height_col,
+    int width_col, int kernel_h, int kernel_w, int pad_h, int pad_w,
+    int stride_h, int stride_w, int dilation_h, int dilation_w,
+    int deformable_group, int offset_last_dim, void *data_col, int dtype,
+    bevk_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Multi-scale deformable attention, forward                                */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * replaces _msda_opt2_musa.forward (csrc_musa/msda/binding_musa.mu:286-412,
+ * :546-549) / ms_deform_attn_forward
+ * (msda_musa_opt2/msda_musa_opt2/dispatch.py:15-35).
+ * All tensors contiguous; spatial_shapes / level_start_index are device
+ * int64 arrays.  im2col_step keeps the reference's contract
+ * (batch % min(batch, im2col_step) == 0, else BEVK_ERR_INVALID_ARGUMENT)
+ * but the whole batch runs in one launch.  value, sampling_loc,
+ * attention_weights and output share dtype (f32, f16 or bf16; f16/bf16
+ * accumulate in fp32).  Every output element is written.
+ */
+BEVK_API int bevk_ms_deform_attn_forward(
+    const void *value, const int64_t *spatial_shapes,
+    const int64_t *level_start_index, const void *sampling_loc,
+    const void *attention_weights, int batch, int spatial_size, int num_heads,
+    int channels, int num_levels, int num_query, int num_point,
+    int im2col_step, void *output, int dtype, bevk_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* BEVK_H_ */

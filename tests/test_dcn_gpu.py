@@ -1,0 +1,219 @@
+"""DCNv2 forward parity on the GPU: CUDA path (through the C ABI and through the
+reference-compatible Python surface) vs the CPU oracle and the reference's own
+golden outputs.
+
+Tolerances (north_star): fp32 within 1e-5 relative L2 and 1e-4 max-abs;
+fp16/bf16 inputs (fp32 accumulation) within 5e-3 relative L2 of the fp32 oracle
+run on the up-cast inputs.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import (FP32_ABS, FP32_REL, HALF_REL, cabi_dcn_forward, dcn_inputs, max_abs,
+                     out_size, rel_l2)
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _golden_cases():
+    return sorted(glob.glob(os.path.join(GOLDEN, "dcn_*.npz")))
+
+
+def _meta(z):
+    kh, kw, sh, sw, ph, pw, dh, dw, groups, dg = (int(v) for v in z["meta"])
+    return (kh, kw), (sh, sw), (ph, pw), (dh, dw), groups, dg
+
+
+def _oracle(x, off, mask, w, b, stride, pad, dil, groups=1, dg=1):
+    return torch.from_numpy(oracle.dcn_forward(
+        x.float().cpu().numpy(), off.float().cpu().numpy(), mask.float().cpu().numpy(),
+        w.float().cpu().numpy(), None if b is None else b.float().cpu().numpy(),
+        stride, pad, dil, groups, dg))
+
+
+def _watchdog_clean():
+    from bevk import cabi
+    import ctypes
+    code = ctypes.c_uint(0)
+    st = cabi.lib().bevk_device_watchdog(0, ctypes.byref(code))
+    assert st == 0 and code.value == 0, f"device watchdog fired: 0x{code.value:x}"
+
+
+@pytest.mark.parametrize("path", _golden_cases(), ids=lambda p: os.path.basename(p)[:-4])
+def test_golden_fp32_cabi(cuda, path):
+    """fp32 exact path vs the reference's own golden (NCHW im2col + mm)."""
+    z = np.load(path)
+    k, st, pd, dl, groups, dg = _meta(z)
+    x, off, mask, w = (torch.from_numpy(z[n]).to(cuda) for n in ("x", "offset", "mask", "weight"))
+    b = torch.from_numpy(z["bias"]).to(cuda) if "bias" in z else None
+    ref = torch.from_numpy(z["out"])
+    out = torch.empty_like(ref, device=cuda)
+    cabi_dcn_forward(x, off, mask, w, b, out, st, pd, dl, groups, dg)
+    torch.cuda.synchronize()
+    assert rel_l2(out, ref) <= FP32_REL and max_abs(out, ref) <= FP32_ABS
+    _watchdog_clean()
+
+
+@pytest.mark.parametrize("path", _golden_cases(), ids=lambda p: os.path.basename(p)[:-4])
+def test_golden_function_surface(cuda, path):
+    """ModulatedDeformConv2dFunction.apply (reference argument order) vs golden."""
+    from modulated_deform_conv import modulated_deform_conv2d
+    z = np.load(path)
+    k, st, pd, dl, groups, dg = _meta(z)
+    x, off, mask, w = (torch.from_numpy(z[n]).to(cuda) for n in ("x", "offset", "mask", "weight"))
+    b = torch.from_numpy(z["bias"]).to(cuda) if "bias" in z else None
+    out = modulated_deform_conv2d(x, off, mask, w, b, st, pd, dl, groups, dg)
+    assert out.is_contiguous() and out.dtype == torch.float32
+    ref = torch.from_numpy(z["out"])
+    assert rel_l2(out, ref) <= FP32_REL and max_abs(out, ref) <= FP32_ABS
+
+
+@pytest.mark.parametrize("path", [p for p in _golden_cases() if "groups" not in p],
+                         ids=lambda p: os.path.basename(p)[:-4])
+def test_golden_nhwc_half(cuda, path):
+    """Tensor-core path (fp16/bf16, NHWC input and output) vs the reference's NHWC golden."""
+    from modulated_deform_conv import dcn_forward_into
+    z = np.load(path)
+    k, st, pd, dl, groups, dg = _meta(z)
+    ref = torch.from_numpy(z["out_nhwc"])
+    for dt in (torch.float16, torch.bfloat16):
+        x = torch.from_numpy(z["x"]).to(cuda, dt)
+        off = torch.from_numpy(z["offset"]).to(cuda, dt)
+        mask = torch.from_numpy(z["mask"]).to(cuda, dt)
+        w = torch.from_numpy(z["weight"]).to(cuda, dt)
+        b = torch.from_numpy(z["bias"]).to(cuda, dt) if "bias" in z else None
+        # reference of record on the exact (rounded) inputs
+        want = _oracle(x, off, mask, w, b, st, pd, dl).permute(0, 2, 3, 1)
+        x_cl = x.contiguous(memory_format=torch.channels_last)
+        out = torch.empty(ref.shape, dtype=dt, device=cuda)       # [B, Ho, Wo, Cout]
+        dcn_forward_into(x_cl, off, mask, w, b, out.permute(0, 3, 1, 2), st, pd, dl)
+        assert rel_l2(out, want) <= HALF_REL, (dt, rel_l2(out, want))
+        assert rel_l2(out, ref) <= 3e-2     # sanity vs the fp32 golden of the unrounded data
+
+
+TC_CASES = [
+    # B, C, H, W, Cout, k, stride, pad, dil, off_std, big_frac
+    (1, 64, 9, 17, 64, (3, 3), (1, 1), (1, 1), (1, 1), 2.0, 0.0),
+    (2, 8, 7, 5, 16, (3, 3), (1, 1), (1, 1), (1, 1), 2.0, 0.0),
+    (1, 72, 11, 13, 96, (3, 3), (1, 1), (1, 1), (1, 1), 2.0, 0.05),
+    (2, 128, 10, 19, 320, (3, 3), (2, 2), (1, 1), (1, 1), 1.0, 0.0),
+    (1, 24, 15, 9, 40, (3, 3), (1, 2), (2, 1), (2, 1), 3.0, 0.0),
+    (3, 256, 8, 12, 256, (3, 3), (1, 1), (1, 1), (1, 1), 2.0, 0.05),
+    (1, 40, 9, 9, 130, (1, 3), (1, 1), (0, 1), (1, 1), 1.0, 0.0),
+]
+
+
+@pytest.mark.parametrize("case", TC_CASES, ids=[f"tc{i}" for i in range(len(TC_CASES))])
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("layout", ["nchw_in", "nhwc_in"])
+def test_tensor_core_path(cuda, case, dt, layout):
+    B, C, H, W, Cout, k, stride, pad, dil, off_std, big = case
+    x, off, mask, w, b = dcn_inputs(11, B, C, H, W, Cout, k, stride, pad, dil, off_std=off_std,
+                                    big_frac=big)
+    x, off, mask, w, b = (t.to(cuda, dt) for t in (x, off, mask, w, b))
+    want = _oracle(x, off, mask, w, b, stride, pad, dil)
+    if layout == "nhwc_in":
+        x = x.contiguous(memory_format=torch.channels_last)
+        out = torch.empty(want.shape, dtype=dt, device=cuda,
+                          memory_format=torch.channels_last)
+    else:
+        out = torch.empty(want.shape, dtype=dt, device=cuda)
+    cabi_dcn_forward(x, off, mask, w, b, out, stride, pad, dil)
+    torch.cuda.synchronize()
+    assert rel_l2(out, want) <= HALF_REL, rel_l2(out, want)
+    _watchdog_clean()
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_fused_logit_mask(cuda, dt):
+    """Raw offset-conv output y (offsets + pre-sigmoid mask, NHWC) read directly."""
+    from modulated_deform_conv import dcn_forward_into
+    B, C, H, W, Cout = 2, 64, 12, 14, 128
+    x, off, mask, w, b = dcn_inputs(5, B, C, H, W, Cout)
+    logits = torch.logit(mask)
+    y = torch.cat([off, logits], 1).to(cuda, dt).contiguous(memory_format=torch.channels_last)
+    xd, wd, bd = x.to(cuda, dt), w.to(cuda, dt), b.to(cuda, dt)
+    want = _oracle(xd, y[:, :18], torch.sigmoid(y[:, 18:].float()), wd, bd, 1, 1, 1)
+    out = torch.empty(want.shape, dtype=dt, device=cuda)
+    dcn_forward_into(xd.contiguous(memory_format=torch.channels_last), y[:, :18], y[:, 18:], wd,
+                     bd, out, 1, 1, 1, mask_is_logit=True)
+    assert rel_l2(out, want) <= HALF_REL
+
+
+@pytest.mark.parametrize("cfg", ["cfg2", "cfg3"])
+def test_baseline_configs_full_size(cuda, cfg):
+    """BASELINE configs 2 and 3 at full size (NHWC, fp16 / bf16) vs the oracle."""
+    from modulated_deform_conv import dcn_forward_into
+    if cfg == "cfg2":
+        B, C, H, W, Cout, dt, big = 6, 512, 29, 50, 512, torch.float16, 0.0
+    else:
+        B, C, H, W, Cout, dt, big = 6, 256, 58, 100, 256, torch.bfloat16, 0.05
+    x, off, mask, w, _ = dcn_inputs(2026, B, C, H, W, Cout, off_std=2.0, big_frac=big, bias=False)
+    x, off, mask, w = (t.to(cuda, dt) for t in (x, off, mask, w))
+    want = _oracle(x, off, mask, w, None, 1, 1, 1)
+    x_cl = x.contiguous(memory_format=torch.channels_last)
+    out = torch.empty(B, Cout, H, W, dtype=dt, device=cuda, memory_format=torch.channels_last)
+    dcn_forward_into(x_cl, off, mask, w, None, out, 1, 1, 1)
+    torch.cuda.synchronize()
+    assert rel_l2(out, want) <= HALF_REL, rel_l2(out, want)
+    _watchdog_clean()
+
+
+def test_fp64_and_grouped_simt(cuda):
+    x, off, mask, w, b = dcn_inputs(3, 2, 12, 9, 8, 18, groups=3, dg=2, off_std=1.5)
+    x, off, mask, w, b = (t.double().to(cuda) for t in (x, off, mask, w, b))
+    want = _oracle(x, off, mask, w, b, 1, 1, 1, groups=3, dg=2)
+    out = torch.empty(want.shape, dtype=torch.float64, device=cuda)
+    cabi_dcn_forward(x, off, mask, w, b, out, (1, 1), (1, 1), (1, 1), groups=3, dg=2)
+    assert rel_l2(out, want) <= FP32_REL
+
+
+def test_im2col_compat_ops(cuda):
+    """Reference extension column ops vs the reference goldens' column matrices."""
+    import _modulated_deform_conv_ext as ext
+    for path in _golden_cases():
+        z = np.load(path)
+        if "columns_nchw" not in z:
+            continue
+        (kh, kw), (sh, sw), (ph, pw), (dh, dw), groups, dg = _meta(z)
+        x, off, mask = (torch.from_numpy(z[n]).to(cuda) for n in ("x", "offset", "mask"))
+        B, C, H, W = x.shape
+        Ho, Wo = out_size(H, ph, dh, kh, sh), out_size(W, pw, dw, kw, sw)
+        col = torch.empty(C * kh * kw, B * Ho * Wo, device=cuda)
+        for fn in (ext.modulated_deformable_im2col_cuda, ext.modulated_deformable_im2col_opt_cuda):
+            col.fill_(float("nan"))
+            fn(x, off, mask, B, C, H, W, Ho, Wo, kh, kw, ph, pw, sh, sw, dh, dw, dg, col)
+            ref = torch.from_numpy(z["columns_nchw"])
+            assert rel_l2(col, ref) <= FP32_REL and max_abs(col, ref) <= FP32_ABS
+        if "columns_nhwc" in z:
+            T = kh * kw
+            xn = x.permute(0, 2, 3, 1).contiguous()
+            offn = off.permute(0, 2, 3, 1).contiguous()
+            mkn = mask.permute(0, 2, 3, 1).contiguous()
+            coln = torch.full((B * Ho * Wo, T * C), float("nan"), device=cuda)
+            ext.modulated_deformable_im2col_nhwc_cuda(xn, offn, mkn, B, C, H, W, Ho, Wo, kh, kw,
+                                                      ph, pw, sh, sw, dh, dw, 1, coln)
+            ref = torch.from_numpy(z["columns_nhwc"])
+            assert rel_l2(coln, ref) <= FP32_REL and max_abs(coln, ref) <= FP32_ABS
+            # fused y [B, Ho, Wo, 3T]: offsets + pre-sigmoid mask
+            y = torch.cat([offn, torch.logit(mkn.double()).float()], -1).contiguous()
+            coln.fill_(float("nan"))
+            ext.modulated_deformable_im2col_nhwc_cuda(xn, y, y, B, C, H, W, Ho, Wo, kh, kw,
+                                                      ph, pw, sh, sw, dh, dw, 1, coln)
+            assert rel_l2(coln, ref) <= FP32_REL
+
+
+def test_errors_are_raised(cuda):
+    from modulated_deform_conv import modulated_deform_conv2d
+    x, off, mask, w, b = (t.to(cuda) for t in dcn_inputs(1, 1, 8, 6, 6, 8))
+    with pytest.raises(RuntimeError):
+        modulated_deform_conv2d(x, off[:, :10], mask, w, b, 1, 1, 1)      # wrong offset channels
+    with pytest.raises(RuntimeError):
+        modulated_deform_conv2d(x, off, mask, w, b, 1, 1, 1, 3, 1)        # groups must divide

@@ -1,0 +1,88 @@
+"""MSDA forward parity on the GPU (C ABI and Python surface) vs the CPU oracle.
+
+Tolerances: fp32 within 1e-5 relative L2 and 1e-4 max-abs; fp16/bf16 within
+5e-3 relative L2 of the fp32 oracle on the up-cast inputs.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import (FP32_ABS, FP32_REL, HALF_REL, cabi_msda_forward, max_abs, msda_inputs,
+                     rel_l2)
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+CFG4 = dict(B=2, shapes=[(200, 200)], M=8, C=32, Q=40000, P=4)
+CFG5 = dict(B=6, shapes=[(116, 200), (58, 100), (29, 50), (15, 25)], M=8, C=32, Q=10000, P=8)
+
+
+def _oracle(value, shapes, lsi, loc, attn):
+    return torch.from_numpy(oracle.msda_forward(value.float().cpu().numpy(), shapes.cpu().numpy(),
+                                                lsi.cpu().numpy(), loc.float().cpu().numpy(),
+                                                attn.float().cpu().numpy()))
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "msda_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[:-4])
+def test_fixtures_cabi(cuda, path):
+    z = np.load(path)
+    value, shapes, lsi, loc, attn = (torch.from_numpy(z[n]).to(cuda) for n in (
+        "value", "spatial_shapes", "level_start_index", "sampling_loc", "attn_weight"))
+    out = cabi_msda_forward(value, shapes, lsi, loc, attn)
+    ref = torch.from_numpy(z["out"])
+    assert rel_l2(out, ref) <= FP32_REL and max_abs(out, ref) <= FP32_ABS
+
+
+SMALL = [
+    dict(B=2, shapes=[(20, 30)], M=8, C=32, Q=300, P=4),
+    dict(B=3, shapes=[(23, 41), (12, 21), (6, 11), (3, 6)], M=8, C=32, Q=257, P=8),
+    dict(B=1, shapes=[(9, 7), (5, 4)], M=4, C=32, Q=100, P=13),      # L*P > 32 samples
+    dict(B=2, shapes=[(10, 12), (5, 6)], M=3, C=24, Q=50, P=3),      # generic kernel (C != 32)
+    dict(B=1, shapes=[(1, 1), (2, 1)], M=8, C=32, Q=40, P=2),        # degenerate levels
+]
+
+
+@pytest.mark.parametrize("cfg", SMALL, ids=[f"s{i}" for i in range(len(SMALL))])
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16],
+                         ids=["f32", "f16", "bf16"])
+def test_small_cases(cuda, cfg, dt):
+    value, shapes, lsi, loc, attn = msda_inputs(7, oob_frac=0.1, **cfg)
+    value, loc, attn = (t.to(cuda, dt) for t in (value, loc, attn))
+    shapes, lsi = shapes.to(cuda), lsi.to(cuda)
+    want = _oracle(value, shapes, lsi, loc, attn)
+    out = cabi_msda_forward(value, shapes, lsi, loc, attn)
+    if dt == torch.float32:
+        assert rel_l2(out, want) <= FP32_REL and max_abs(out, want) <= FP32_ABS
+    else:
+        assert out.dtype == dt and rel_l2(out, want) <= HALF_REL
+
+
+@pytest.mark.parametrize("name", ["cfg4", "cfg5"])
+def test_baseline_configs_full_size(cuda, name):
+    import ms_deform_attn
+    cfg = CFG4 if name == "cfg4" else CFG5
+    value, shapes, lsi, loc, attn = msda_inputs(2026, oob_frac=0.02 if name == "cfg4" else 0.0,
+                                                **cfg)
+    want = _oracle(value, shapes, lsi, loc, attn)
+    value, shapes, lsi, loc, attn = (t.to(cuda) for t in (value, shapes, lsi, loc, attn))
+    out = ms_deform_attn.MultiScaleDeformableAttnFunction.apply(value, shapes, lsi, loc, attn, 64)
+    assert out.shape == (cfg["B"], cfg["Q"], cfg["M"] * cfg["C"])
+    assert rel_l2(out, want) <= FP32_REL and max_abs(out, want) <= FP32_ABS
+
+
+def test_im2col_step_contract(cuda):
+    import ms_deform_attn
+    value, shapes, lsi, loc, attn = (t.to(cuda) for t in msda_inputs(1, 3, [(6, 6)], 8, 32, 10, 4))
+    with pytest.raises(RuntimeError, match="im2col_step"):
+        ms_deform_attn.ms_deform_attn_forward(value, shapes, lsi, loc, attn, im2col_step=2)
+    out = ms_deform_attn.ms_deform_attn_forward(value, shapes, lsi, loc, attn, im2col_step=3)
+    want = _oracle(value, shapes, lsi, loc, attn)
+    assert rel_l2(out, want) <= FP32_REL
+    with pytest.raises(RuntimeError, match="contiguous"):
+        ms_deform_attn.ms_deform_attn_forward(value.transpose(1, 2), shapes, lsi, loc, attn)

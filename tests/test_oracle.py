@@ -1,0 +1,125 @@
+"""CPU oracle pinned against the reference's own goldens (tests/golden) and
+cross-checked against independent formulations.  No GPU needed."""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from oracle.msda_grid_sample import msda_forward_grid_sample
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+DCN_FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "dcn_*.npz")))
+MSDA_FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "msda_*.npz")))
+
+
+def _meta(z):
+    kh, kw, sh, sw, ph, pw, dh, dw, groups, dg = (int(v) for v in z["meta"])
+    return (kh, kw), (sh, sw), (ph, pw), (dh, dw), groups, dg
+
+
+def test_fixture_set_present():
+    names = {os.path.basename(p) for p in DCN_FIXTURES + MSDA_FIXTURES}
+    assert "dcn_cfg1.npz" in names and len(DCN_FIXTURES) >= 6 and len(MSDA_FIXTURES) >= 2
+
+
+@pytest.mark.parametrize("path", DCN_FIXTURES, ids=lambda p: os.path.basename(p)[:-4])
+def test_dcn_forward_matches_reference_golden(path):
+    """oracle vs modulated_deformable_im2col_pytorch + grouped mm (the reference's golden)."""
+    z = np.load(path)
+    k, st, pd, dl, groups, dg = _meta(z)
+    out = oracle.dcn_forward(z["x"], z["offset"], z["mask"], z["weight"], z.get("bias"),
+                             st, pd, dl, groups, dg)
+    assert oracle.rel_l2(out, z["out"]) <= 1e-6
+    assert oracle.max_abs(out, z["out"]) <= 1e-5
+
+
+@pytest.mark.parametrize("path", [p for p in DCN_FIXTURES if "groups" not in p],
+                         ids=lambda p: os.path.basename(p)[:-4])
+def test_dcn_nhwc_golden(path):
+    """oracle vs the reference's NHWC golden (fused_tl.dcn_forward_golden_nhwc)."""
+    z = np.load(path)
+    k, st, pd, dl, groups, dg = _meta(z)
+    out = oracle.dcn_forward(z["x"], z["offset"], z["mask"], z["weight"], z.get("bias"),
+                             st, pd, dl)
+    assert oracle.rel_l2(out.transpose(0, 2, 3, 1), z["out_nhwc"]) <= 1e-6
+
+
+@pytest.mark.parametrize("path", [p for p in DCN_FIXTURES if "columns_nchw" in np.load(p)],
+                         ids=lambda p: os.path.basename(p)[:-4])
+def test_dcn_columns_match_reference(path):
+    z = np.load(path)
+    k, st, pd, dl, groups, dg = _meta(z)
+    col = oracle.dcn_columns(z["x"], z["offset"], z["mask"], k, st, pd, dl, dg, layout="nchw")
+    assert oracle.max_abs(col, z["columns_nchw"]) <= 1e-5
+    if "columns_nhwc" in z:
+        coln = oracle.dcn_columns(z["x"], z["offset"], z["mask"], k, st, pd, dl, dg,
+                                  layout="nhwc")
+        assert oracle.max_abs(coln, z["columns_nhwc"]) <= 1e-5
+
+
+def test_dcn_matches_torchvision():
+    """Third formulation: torchvision.ops.deform_conv2d (bit-identical to the
+    reference golden at config 1 in the survey probe)."""
+    tv = pytest.importorskip("torchvision")
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(2, 16, 11, 9, generator=g)
+    w = torch.randn(12, 16, 3, 3, generator=g)
+    off = torch.randn(2, 18, 6, 5, generator=g) * 2
+    m = torch.rand(2, 9, 6, 5, generator=g)
+    b = torch.randn(12, generator=g)
+    want = tv.ops.deform_conv2d(x, off, w, b, stride=2, padding=1, dilation=1, mask=m)
+    got = oracle.dcn_forward(x.numpy(), off.numpy(), m.numpy(), w.numpy(), b.numpy(), 2, 1, 1)
+    assert oracle.rel_l2(got, want.numpy()) <= 1e-6
+
+
+def test_dcn_pixel_range_is_a_slice():
+    z = np.load(DCN_FIXTURES[0])
+    k, st, pd, dl, groups, dg = _meta(z)
+    full = oracle.dcn_forward(z["x"], z["offset"], z["mask"], z["weight"], z.get("bias"),
+                              st, pd, dl, groups, dg)
+    part = oracle.dcn_forward(z["x"], z["offset"], z["mask"], z["weight"], z.get("bias"),
+                              st, pd, dl, groups, dg, pix_range=(100, 300))
+    B, C, Ho, Wo = full.shape
+    flat_full = full.transpose(0, 2, 3, 1).reshape(-1, C)
+    flat_part = part.transpose(0, 2, 3, 1).reshape(-1, C)
+    assert np.array_equal(flat_part[100:300], flat_full[100:300])
+    assert not flat_part[:100].any() and not flat_part[300:].any()
+
+
+@pytest.mark.parametrize("path", MSDA_FIXTURES, ids=lambda p: os.path.basename(p)[:-4])
+def test_msda_matches_fixture(path):
+    z = np.load(path)
+    out = oracle.msda_forward(z["value"], z["spatial_shapes"], z["level_start_index"],
+                              z["sampling_loc"], z["attn_weight"])
+    assert oracle.rel_l2(out, z["out"]) <= 1e-6
+
+
+def test_msda_matches_grid_sample_random():
+    g = torch.Generator().manual_seed(11)
+    shapes = [(13, 17), (7, 9), (4, 5)]
+    sizes = [h * w for h, w in shapes]
+    lsi = np.concatenate([[0], np.cumsum(sizes)[:-1]])
+    B, M, C, Q, P = 2, 4, 16, 64, 5
+    value = torch.randn(B, sum(sizes), M, C, generator=g)
+    loc = torch.rand(B, Q, M, 3, P, 2, generator=g) * 1.5 - 0.25      # many points outside
+    attn = torch.rand(B, Q, M, 3, P, generator=g)
+    want = msda_forward_grid_sample(value, torch.tensor(shapes), loc, attn).numpy()
+    got = oracle.msda_forward(value.numpy(), np.array(shapes), lsi, loc.numpy(), attn.numpy())
+    assert oracle.rel_l2(got, want) <= 1e-6 and oracle.max_abs(got, want) <= 1e-5
+
+
+def test_msda_boundary_coordinates():
+    """Points exactly on the gates: h = -1 and h = H (dropped), h = H-1 (kept)."""
+    H, W = 4, 5
+    value = np.arange(H * W * 1 * 1, dtype=np.float32).reshape(1, H * W, 1, 1) + 1
+    # loc_y*H - 0.5 = -1  -> loc_y = -0.5/H ; = H -> (H+0.5)/H ; = H-1 -> (H-0.5)/H
+    ys = np.array([-0.5 / H, (H + 0.5) / H, (H - 0.5) / H], np.float32)
+    loc = np.zeros((1, 3, 1, 1, 1, 2), np.float32)
+    loc[0, :, 0, 0, 0, 0] = 0.5            # x in range
+    loc[0, :, 0, 0, 0, 1] = ys
+    attn = np.ones((1, 3, 1, 1, 1), np.float32)
+    out = oracle.msda_forward(value, [[H, W]], [0], loc, attn)
+    assert out[0, 0, 0] == 0 and out[0, 1, 0] == 0 and out[0, 2, 0] != 0

@@ -1,0 +1,97 @@
+"""Operator-surface host logic on CPU: module construction and checkpoint
+compatibility, exported names, argument checks, and no CPU fallback."""
+import pytest
+import torch
+
+import modulated_deform_conv as mdc
+import ms_deform_attn
+
+
+def test_reference_exports_present():
+    for name in ("ModulatedDeformConv2dFunction", "ModulatedDeformConv2d",
+                 "ModulatedDeformConv2dPack", "modulated_deform_conv2d", "dcn_apply_nchw",
+                 "dcn_split_nhwc", "gather_cols_nhwc", "DCNSplitNHWCFunction"):
+        assert hasattr(mdc, name), name
+    import msda_musa_opt2
+    assert msda_musa_opt2.ms_deform_attn_forward is ms_deform_attn.ms_deform_attn_forward
+    assert hasattr(ms_deform_attn, "MultiScaleDeformableAttnFunction")
+
+
+def test_extension_exports_reference_op_names():
+    import _modulated_deform_conv_ext as ext
+    for name in ("modulated_deformable_im2col_cuda", "modulated_deformable_im2col_opt_cuda",
+                 "modulated_deformable_im2col_nhwc_cuda", "dcn_forward", "dcn_pack_weight"):
+        assert hasattr(ext, name), name
+    import _ms_deform_attn_ext as mext
+    assert hasattr(mext, "forward")
+
+
+def test_module_parameters_match_mmcv_layout():
+    m = mdc.ModulatedDeformConv2dPack(64, 32, 3, stride=1, padding=1, deform_groups=2,
+                                      bias=False)
+    sd = m.state_dict()
+    assert set(sd) == {"weight", "conv_offset.weight", "conv_offset.bias"}
+    assert sd["weight"].shape == (32, 64, 3, 3)
+    assert sd["conv_offset.weight"].shape == (2 * 3 * 9, 64, 3, 3)
+    assert torch.count_nonzero(sd["conv_offset.weight"]) == 0      # zero-initialised offsets
+    m2 = mdc.ModulatedDeformConv2d(16, 8, (3, 1), groups=2)
+    assert m2.weight.shape == (8, 8, 3, 1) and m2.bias.shape == (8,)
+    assert float(m2.weight.detach().abs().max()) <= 1.0 / (16 * 3) ** 0.5 + 1e-7
+
+
+def test_state_dict_v1_offset_key_migration():
+    """Version-1 checkpoints name the offset conv "<prefix>_offset"; loading renames
+    the keys to conv_offset (modulated_deform_conv.py:629-643).  Torch filters the
+    state dict per child prefix, so the rename applies where the module is the root
+    of the load, exactly as in the reference."""
+    m = mdc.ModulatedDeformConv2dPack(8, 8, 3, padding=1)
+    sd = {k: v.clone() for k, v in m.state_dict().items()}
+    w = torch.randn_like(sd["conv_offset.weight"])
+    b = torch.randn_like(sd["conv_offset.bias"])
+    old = torch.nn.modules.module.OrderedDict(
+        [("weight", sd["weight"]), ("bias", sd["bias"]), ("_offset.weight", w),
+         ("_offset.bias", b)])
+    old._metadata = {"": {"version": 1}}
+    m.load_state_dict(old)
+    assert torch.equal(m.conv_offset.weight, w) and torch.equal(m.conv_offset.bias, b)
+
+
+def test_backend_kwarg_accepted(monkeypatch):
+    monkeypatch.setenv("DCN_BACKEND", "tilelang")
+    m = mdc.ModulatedDeformConv2dPack(8, 8, 3, padding=1, backend="cuda")
+    assert m.backend == "cuda"
+    m2 = mdc.ModulatedDeformConv2dPack(8, 8, 3, padding=1)
+    assert m2.backend == "tilelang"
+
+
+def test_no_cpu_fallback():
+    x = torch.randn(1, 8, 6, 6)
+    off = torch.zeros(1, 18, 6, 6)
+    mask = torch.ones(1, 9, 6, 6)
+    w = torch.randn(8, 8, 3, 3)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        mdc.modulated_deform_conv2d(x, off, mask, w, None, 1, 1, 1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ms_deform_attn.ms_deform_attn_forward(torch.randn(1, 4, 1, 32),
+                                              torch.tensor([[2, 2]]), torch.tensor([0]),
+                                              torch.rand(1, 3, 1, 1, 1, 2),
+                                              torch.rand(1, 3, 1, 1, 1))
+
+
+def test_function_rejects_non_4d_input():
+    with pytest.raises(ValueError):
+        mdc.modulated_deform_conv2d(torch.randn(8, 6, 6), torch.zeros(1), torch.zeros(1),
+                                    torch.zeros(1, 8, 3, 3))
+
+
+def test_sharding_blocks_cover_exactly():
+    from bevk.sharding import shard_range
+    for n in (48, 7, 1, 0):
+        for world in (1, 2, 4, 8):
+            blocks = [shard_range(n, r, world) for r in range(world)]
+            assert blocks[0][0] == 0 and blocks[-1][1] == n
+            assert all(b[1] == c[0] for b, c in zip(blocks, blocks[1:]))
+            sizes = [e - b for b, e in blocks]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_range(4, 2, 2)
