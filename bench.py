@@ -453,6 +453,9 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--only", choices=("cfg2", "cfg3", "cfg4", "cfg5"),
+                    help="time one workload's kernel only (profiling runs: no e2e, "
+                         "secondary or CPU legs; prints a reduced line)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -478,6 +481,21 @@ def main():
     stream = torch.cuda.Stream(device=device)
     peaks, peaks_src = _peaks()
     seed = 2026
+
+    if args.only:
+        if args.only in DCN_CFGS:
+            r = bench_dcn(args.only, args.steps, args.warmup, device, seed, 0, stream, dist)
+            del r["sets"]
+            extra = {"tflops": r["flops"] / r["per_launch_s"] / 1e12}
+        else:
+            r = bench_msda(args.only, args.steps, args.warmup, device, seed, stream)
+            extra = {"algorithmic_GBps": r["bytes"] / r["per_launch_s"] / 1e9}
+        if rank == 0:
+            print(json.dumps({"profile_run": True, "workload": args.only,
+                              "us_per_call": r["per_launch_s"] * 1e6, **extra}), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     # headline: cfg2 DCN, this rank's 6 cameras are global images [6*rank, 6*rank+6)
     clocks = ClockSampler(local_rank)
