@@ -23,6 +23,9 @@ ERR_CUDA = -5
 ERR_WORKSPACE = -6
 ERR_DEVICE_TIMEOUT = -7
 
+# Size of the scratch array behind bevk_dcn_forward_noalloc (BEVK_DCN_NOALLOC_SCRATCH_BYTES).
+DCN_NOALLOC_SCRATCH_BYTES = 32 << 20
+
 # Every exported symbol of include/bevk.h.
 EXPORTED_SYMBOLS = (
     "bevk_version",
@@ -34,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "bevk_dcn_pack_weight",
     "bevk_dcn_forward_workspace_bytes",
     "bevk_dcn_forward",
+    "bevk_dcn_forward_noalloc",
     "bevk_modulated_deformable_im2col",
     "bevk_modulated_deformable_im2col_opt",
     "bevk_modulated_deformable_im2col_nhwc",
@@ -97,6 +101,8 @@ def lib():
     L.bevk_dcn_forward_workspace_bytes.argtypes = [pp]
     L.bevk_dcn_forward.restype = i
     L.bevk_dcn_forward.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp, sz, vp]
+    L.bevk_dcn_forward_noalloc.restype = i
+    L.bevk_dcn_forward_noalloc.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp]
     col_args = [vp, vp, vp] + [i] * 15
     L.bevk_modulated_deformable_im2col.restype = i
     L.bevk_modulated_deformable_im2col.argtypes = col_args + [vp, i, vp]

@@ -140,6 +140,34 @@ BEVK_API int bevk_dcn_forward(const bevk_dcn_problem *p, const void *input,
                               size_t workspace_bytes, bevk_stream_t stream);
 
 /*
+ * Allocation-free variant of bevk_dcn_forward.  No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc or hand out a
+ * workspace at the moment they run the layer -- an inference engine's plugin
+ * whose enqueue step may not allocate and was promised no workspace, or a
+ * runtime that freezes device memory after start-up for determinism.
+ *
+ * Takes the unpacked weight [Cout, Cin/groups, kH, kW] (contiguous) and does
+ * the weight packing and, for NCHW input on the tensor-core path, the NHWC
+ * copy of the input inside a fixed scratch array that the library itself
+ * holds in device memory: BEVK_DCN_NOALLOC_SCRATCH_BYTES per GPU on which the
+ * library's code is loaded, kept until the process exits.  Problems needing
+ * more than that (packed weight, rounded up to 256 bytes, plus the input copy
+ * when one is needed) return BEVK_ERR_WORKSPACE without launching anything.
+ *
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before capturing
+ * a stream into a CUDA graph.  All calls on a device share the one array and
+ * its contents persist between calls (nothing in it needs to start at zero):
+ * calls whose kernels can overlap on the GPU -- different streams without
+ * ordering between them -- race on it, so serialise them.
+ */
+#define BEVK_DCN_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+BEVK_API int bevk_dcn_forward_noalloc(const bevk_dcn_problem *p, const void *input,
+                                      const void *offset, const void *mask,
+                                      const void *weight, const void *bias, void *output,
+                                      bevk_stream_t stream);
+
+/*
  * Column-matrix ops of the reference extension (binding names kept).
  *
  * bevk_modulated_deformable_im2col / _opt replace
