@@ -48,7 +48,8 @@ namespace {
 
 constexpr int kBM = 128;           // pixels per tile (UMMA M)
 constexpr int kBK = 64;            // channels per stage (128 B of fp16/bf16)
-constexpr int kGatherWarps = 8;
+constexpr int kGatherWarps = 16;
+constexpr int kRowsPerThread = kBM / (kGatherWarps * 4);  // 8 lanes per row, 4 rows per warp pass
 constexpr int kThreads = (kGatherWarps + 2) * 32;
 constexpr int kTmaWarp = kGatherWarps;
 constexpr int kMmaWarp = kGatherWarps + 1;
@@ -246,52 +247,96 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
     ptx::named_barrier_sync(1, kGatherWarps * 32);
 
     // ---------------------------------------------------------- gather
+    // Each thread owns kRowsPerThread rows x one 16-byte channel chunk of every
+    // stage.  The four corner loads of all its rows for stage k+1 are issued
+    // (predicated, into registers) before stage k is interpolated and stored,
+    // so a full stage of corner reads is always in flight per thread.  Stage
+    // coordinates advance incrementally (no integer division in the loop).
     const int j = lane & 7;     // 16-byte chunk (8 channels) within the 128-byte row
     const int rsub = lane >> 3; // row within the warp's group of 4
     const int xs2 = p.xs2, xs3 = p.xs3;
-    bool ok = true;
-    for (int kit = 0; kit < p.n_k && ok; ++kit) {
-      const int s = kit % STAGES;
-      const uint32_t ph = (kit / STAGES) & 1;
-      ok = ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1, s_abort, &g_bevk_watchdog,
-                                  kSiteGatherEmpty);
-      if (!ok) break;
-      const int t = p.tap_major ? kit / p.n_cc : kit % p.T;
-      const int cc = p.tap_major ? kit - (kit / p.n_cc) * p.n_cc : kit / p.T;
-      const int c = cc * kBK + j * 8;
-      const bool cvalid = c < p.Cin;
-      const uint32_t a_stage = sA + s * L::kABytes;
+    const int row0 = warp * 4 + rsub;          // rows row0 + i*kGatherWarps*4
+    struct Prefetch {
+      uint4 v[kRowsPerThread][4];
+      int ebase;  // geometry index of the prefetched stage's first row
+    };
+    // (tap, channel chunk) of a stage index, advanced one stage at a time
+    struct StageCoord {
+      int t, cc;
+    };
+    auto next_coord = [&](StageCoord c) {
+      if (p.tap_major) {
+        if (++c.cc == p.n_cc) { c.cc = 0; ++c.t; }
+      } else {
+        if (++c.t == p.T) { c.t = 0; ++c.cc; }
+      }
+      return c;
+    };
+    auto issue = [&](StageCoord sc, Prefetch &P) {
+      const int c = sc.cc * kBK + j * 8;
+      const uint32_t cvalid = c < p.Cin ? 0xFFFFFFFFu : 0u;
+      const int ebase = sc.t * kBM + row0;
+      P.ebase = ebase;
 #pragma unroll
-      for (int i = 0; i < kBM / (kGatherWarps * 4); ++i) {
-        const int r = i * (kGatherWarps * 4) + warp * 4 + rsub;
-        const int e = t * kBM + r;
+      for (int i = 0; i < kRowsPerThread; ++i) {
+        const int e = ebase + i * (kGatherWarps * 4);
         const uint4 wq = s_gw[e];
-        uint4 res = make_uint4(0u, 0u, 0u, 0u);
-        if (cvalid) {
-          const T *px = x + static_cast<int64_t>(s_gb[e]) + c;
-          uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0, v2 = v0, v3 = v0;
-          if (wq.x) v0 = __ldg(reinterpret_cast<const uint4 *>(px));
-          if (wq.y) v1 = __ldg(reinterpret_cast<const uint4 *>(px + xs3));
-          if (wq.z) v2 = __ldg(reinterpret_cast<const uint4 *>(px + xs2));
-          if (wq.w) v3 = __ldg(reinterpret_cast<const uint4 *>(px + xs2 + xs3));
-          res.x = GM::lerp2(wq, v0.x, v1.x, v2.x, v3.x);
-          res.y = GM::lerp2(wq, v0.y, v1.y, v2.y, v3.y);
-          res.z = GM::lerp2(wq, v0.z, v1.z, v2.z, v3.z);
-          res.w = GM::lerp2(wq, v0.w, v1.w, v2.w, v3.w);
-        }
+        const int o = s_gb[e] + c;
+        P.v[i][0] = ptx::ld_global_nc_v4_pred(x + o, wq.x & cvalid);
+        P.v[i][1] = ptx::ld_global_nc_v4_pred(x + (o + xs3), wq.y & cvalid);
+        P.v[i][2] = ptx::ld_global_nc_v4_pred(x + (o + xs2), wq.z & cvalid);
+        P.v[i][3] = ptx::ld_global_nc_v4_pred(x + (o + xs2 + xs3), wq.w & cvalid);
+      }
+    };
+    int cs = 0;          // stage slot of the stage being consumed
+    uint32_t cph = 0;    // its phase
+    auto consume = [&](const Prefetch &P) -> bool {
+      if (!ptx::mbar_wait_bounded(bar_empty + 8 * cs, cph ^ 1, s_abort, &g_bevk_watchdog,
+                                  kSiteGatherEmpty))
+        return false;
+      const uint32_t a_stage = sA + cs * L::kABytes;
+#pragma unroll
+      for (int i = 0; i < kRowsPerThread; ++i) {
+        const int r = row0 + i * (kGatherWarps * 4);
+        const uint4 wq = s_gw[P.ebase + i * (kGatherWarps * 4)];
+        uint4 res;
+        res.x = GM::lerp2(wq, P.v[i][0].x, P.v[i][1].x, P.v[i][2].x, P.v[i][3].x);
+        res.y = GM::lerp2(wq, P.v[i][0].y, P.v[i][1].y, P.v[i][2].y, P.v[i][3].y);
+        res.z = GM::lerp2(wq, P.v[i][0].z, P.v[i][1].z, P.v[i][2].z, P.v[i][3].z);
+        res.w = GM::lerp2(wq, P.v[i][0].w, P.v[i][1].w, P.v[i][2].w, P.v[i][3].w);
         ptx::st_shared_v4(a_stage + r * 128 + ((j ^ (r & 7)) << 4), res);
       }
       ptx::fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_full + 8 * s);
+      if (lane == 0) ptx::mbar_arrive(bar_full + 8 * cs);
+      if (++cs == STAGES) { cs = 0; cph ^= 1; }
+      return true;
+    };
+    bool ok = true;
+    {
+      Prefetch A, B;
+      StageCoord sc{0, 0};
+      if (p.n_k > 0) issue(sc, A);
+      for (int kit = 0; kit < p.n_k; kit += 2) {
+        sc = next_coord(sc);
+        if (kit + 1 < p.n_k) issue(sc, B);
+        ok = consume(A);
+        if (!ok || kit + 1 >= p.n_k) break;
+        sc = next_coord(sc);
+        if (kit + 2 < p.n_k) issue(sc, A);
+        ok = consume(B);
+        if (!ok) break;
+      }
     }
 
     // ---------------------------------------------------------- epilogue
     if (ok) ok = ptx::mbar_wait_bounded(bar_tmem, 0, s_abort, &g_bevk_watchdog, kSiteEpilogue);
     if (ok) {
       ptx::tc_fence_after();
-      const int q = warp & 3;          // TMEM lane quadrant of this warp
-      const int half = warp >> 2;      // which half of the BN columns
+      constexpr int kColsPerWarp = BN / 4;           // 4 warps share each TMEM lane quadrant
+      constexpr int kChunk = kColsPerWarp < 32 ? kColsPerWarp : 32;
+      const int q = warp & 3;                        // TMEM lane quadrant of this warp
+      const int cgrp = warp >> 2;                    // which quarter of the BN columns
       const int row = q * 32 + lane;
       const int m = m0 + row;
       const int HoWo = p.Ho * p.Wo;
@@ -302,23 +347,23 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
                            (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (p.ys[0] & 7) == 0 &&
                            (p.ys[2] & 7) == 0 && (p.ys[3] & 7) == 0;
 #pragma unroll 1
-      for (int cb = 0; cb < BN / 2; cb += 32) {
-        const int col = half * (BN / 2) + cb;
+      for (int cb = 0; cb < kColsPerWarp; cb += kChunk) {
+        const int col = cgrp * kColsPerWarp + cb;
         if (n0 + col >= p.Cout) break;
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + col, r);
+        uint32_t r[kChunk];
+        ptx::tmem_ld_32x32b<kChunk>(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + col, r);
         ptx::tmem_wait_ld();
         if (m < p.M) {
           const int co0 = n0 + col;
-          float v[32];
+          float v[kChunk];
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
+          for (int jj = 0; jj < kChunk; ++jj) {
             v[jj] = __uint_as_float(r[jj]);
             if (p.has_bias && co0 + jj < p.Cout) v[jj] += ld_float(bias + co0 + jj);
           }
-          if (vec_out && co0 + 32 <= p.Cout) {
+          if (vec_out && co0 + kChunk <= p.Cout) {
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
+            for (int g = 0; g < kChunk / 8; ++g) {
               uint4 pk;
               uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
 #pragma unroll
@@ -329,7 +374,7 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
             }
           } else {
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
+            for (int jj = 0; jj < kChunk; ++jj) {
               if (co0 + jj < p.Cout) {
                 const uint16_t bits = GM::store_bits(v[jj]);
                 *reinterpret_cast<uint16_t *>(yrow + (co0 + jj) * p.ys[1]) = bits;
@@ -505,14 +550,16 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
   if (cr != CUDA_SUCCESS) return fail(BEVK_ERR_CUDA, "dcn tc: tensor map encode failed (%d)", int(cr));
 
   const int nt = static_cast<int>(tiles);
+  // 3 stages: deep enough to overlap gather, TMA and MMA, small enough to leave
+  // ~60 KB of L1 for the corner lines (measured best among 2/3/4).
   if (pr->dtype == BEVK_DTYPE_F16) {
-    if (BN == 256) return launch_tc<__half, 256, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
-    if (BN == 128) return launch_tc<__half, 128, 6>(p, tmap, x, off, msk, bias, y, nt, stream);
-    return launch_tc<__half, 64, 8>(p, tmap, x, off, msk, bias, y, nt, stream);
+    if (BN == 256) return launch_tc<__half, 256, 3>(p, tmap, x, off, msk, bias, y, nt, stream);
+    if (BN == 128) return launch_tc<__half, 128, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
+    return launch_tc<__half, 64, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
   }
-  if (BN == 256) return launch_tc<__nv_bfloat16, 256, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
-  if (BN == 128) return launch_tc<__nv_bfloat16, 128, 6>(p, tmap, x, off, msk, bias, y, nt, stream);
-  return launch_tc<__nv_bfloat16, 64, 8>(p, tmap, x, off, msk, bias, y, nt, stream);
+  if (BN == 256) return launch_tc<__nv_bfloat16, 256, 3>(p, tmap, x, off, msk, bias, y, nt, stream);
+  if (BN == 128) return launch_tc<__nv_bfloat16, 128, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
+  return launch_tc<__nv_bfloat16, 64, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
 }
 
 int read_and_clear_watchdog(int device, unsigned int *code) {
