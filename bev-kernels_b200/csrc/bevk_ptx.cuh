@@ -72,6 +72,60 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// Cluster-scope variants (paired-CTA kernels): a wait that must observe
+// arrivals released by the other CTA of the cluster.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint32_t bar, uint32_t parity,
+                                                          volatile int *abort_flag,
+                                                          unsigned int *err_word,
+                                                          unsigned int site) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 255u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicCAS(err_word, 0u, site);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+// Arrive on an mbarrier given by its shared::cluster address, possibly in the
+// other CTA of the cluster (default release semantics, as CUTLASS's cluster
+// barriers use).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared variable in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+// Whole-cluster execution barrier (all threads of both CTAs), release/acquire.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
 // ---------------------------------------------------------------- proxies
 // Orders this thread's generic-proxy shared-memory writes before subsequent
 // async-proxy reads (tcgen05.mma operands written with st.shared).
@@ -89,6 +143,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void *tmap, uint
                                             int32_t c0, int32_t c1) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Paired-CTA tile load: the copy lands in this CTA's shared memory and its
+// completion bytes are counted on `bar`, which may be the leader CTA's barrier
+// (shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void *tmap, uint32_t bar,
+                                                 int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1)
       : "memory");
@@ -160,6 +226,40 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                : "memory");
 }
 
+// Paired-CTA (cta_group::2) forms: TMEM allocation shared by the two CTAs of
+// a cluster (same warp in each CTA), M=256 MMA issued by the leader CTA, and
+// its completion signalled to the barrier at the same offset in both CTAs.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives once on the barrier at offset `bar` in every CTA of `cta_mask` when
+// the MMAs issued so far by this thread have completed (a commit, not a copy).
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
 // 32 lanes x 32 consecutive 32-bit columns (this warp's lane quadrant).
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -204,13 +304,24 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthread
 // predication instead of a branch lets a thread keep many such loads in flight.
 __device__ __forceinline__ uint4 ld_global_nc_v4_pred(const void *p, uint32_t pred) {
   uint4 v = make_uint4(0u, 0u, 0u, 0u);
-  asm("{\n\t.reg .pred q;\n\t"
+  asm volatile(
+      "{\n\t.reg .pred q;\n\t"
       "setp.ne.b32 q, %4, 0;\n\t"
       "@q ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%5];\n\t}"
       : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
       : "r"(pred), "l"(p));
   return v;
 }
+
+// Scheduling fence on registers: no instruction is emitted, but code using
+// `v` afterwards cannot be hoisted above this point (nor above the volatile
+// loads issued before it).  Used to keep a prefetch ahead of the arithmetic
+// that consumes the previous batch.
+__device__ __forceinline__ void reg_fence(uint4 &v) {
+  asm volatile("" : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w));
+}
+__device__ __forceinline__ void reg_fence(uint2 &v) { asm volatile("" : "+r"(v.x), "+r"(v.y)); }
+__device__ __forceinline__ void reg_fence(float &v) { asm volatile("" : "+f"(v)); }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),

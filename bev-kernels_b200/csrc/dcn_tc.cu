@@ -72,15 +72,17 @@ struct TcParams {
   int64_t os[4], ms[4], ys[4];
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR>
 struct Smem {
+  // In a CTA pair each CTA holds half of the B tile (BN/2 output channels).
+  static constexpr int kBRows = PAIR ? BN / 2 : BN;
   static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kBBytes = kBRows * kBK * 2;
   static constexpr int kA = 0;
   static constexpr int kB = kA + STAGES * kABytes;
   static constexpr int kGW = kB + STAGES * kBBytes;          // uint4 weights [T][BM]
   static constexpr int kGB = kGW + kMaxTaps * kBM * 16;      // int base offsets [T][BM]
-  static constexpr int kBar = kGB + kMaxTaps * kBM * 4;      // full_a[S], full_b[S], empty[S], tmem_full
+  static constexpr int kBar = kGB + kMaxTaps * kBM * 4;      // full[S], wfull[S], empty[S], tmem_full
   static constexpr int kMisc = kBar + (3 * STAGES + 1) * 8;  // tmem slot, abort flag
   static constexpr int kTotal = kMisc + 16;
   static constexpr int kAlloc = kTotal + 1024;               // 1024-byte alignment slack
@@ -186,12 +188,19 @@ __device__ __forceinline__ void tap_geometry(const TcParams &p, const T *__restr
   wq.w = (y1 && x1) ? GatherMath<T>::pack_weight(lh * lw * mk) : 0u;
 }
 
-template <typename T, int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
-dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
-                  const T *__restrict__ x, const T *__restrict__ off, const T *__restrict__ msk,
-                  const T *__restrict__ bias, T *__restrict__ y) {
-  using L = Smem<BN, STAGES>;
+// Kernel body.  PAIR = false: one CTA per 128-pixel tile, M=128 MMA.
+// PAIR = true: a 2-CTA cluster per 256-pixel tile; each CTA gathers its own
+// 128 pixels and TMA-loads half of the weight tile, the leader (rank 0) issues
+// M=256 tcgen05.mma.cta_group::2 reading both CTAs' operands, and each MMA
+// commit releases the stage in both CTAs.  Both CTAs' gather warps and TMA
+// copies report to the leader's barriers.
+template <typename T, int BN, int STAGES, bool PAIR>
+__device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const TcParams &p,
+                                                const T *__restrict__ x,
+                                                const T *__restrict__ off,
+                                                const T *__restrict__ msk,
+                                                const T *__restrict__ bias, T *__restrict__ y) {
+  using L = Smem<BN, STAGES, PAIR>;
   using GM = GatherMath<T>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -209,14 +218,17 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x;
+  const uint32_t cr = PAIR ? ptx::cluster_ctarank() : 0u;   // rank in the CTA pair
+  const bool leader = cr == 0;
+  const int tile = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int n_tile = tile % p.n_tiles_n;
-  const int m0 = (tile / p.n_tiles_n) * kBM;
+  const int m0 = (tile / p.n_tiles_n) * (PAIR ? 2 * kBM : kBM) + static_cast<int>(cr) * kBM;
   const int n0 = n_tile * BN;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      ptx::mbar_init(bar_full + 8 * s, kGatherWarps);      // one arrive per gather warp
+      // one arrive per gather warp (of both CTAs when paired)
+      ptx::mbar_init(bar_full + 8 * s, PAIR ? 2 * kGatherWarps : kGatherWarps);
       ptx::mbar_init(bar_wfull + 8 * s, 1);                // TMA arrive + transaction bytes
       ptx::mbar_init(bar_empty + 8 * s, 1);                // tcgen05.commit
     }
@@ -224,15 +236,29 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
     *s_abort = 0;
     ptx::fence_mbar_init();
   }
+  // Paired CTAs: every barrier of both CTAs is initialised before any
+  // cross-CTA arrive or copy can target it.
+  if constexpr (PAIR) ptx::cluster_sync();
   if (warp == kMmaWarp) {
-    ptx::tmem_alloc(ptx::smem_u32(s_tmem_slot), BN);
-    ptx::tmem_relinquish();
+    if constexpr (PAIR) {
+      ptx::tmem_alloc_pair(ptx::smem_u32(s_tmem_slot), BN);
+      ptx::tmem_relinquish_pair();
+    } else {
+      ptx::tmem_alloc(ptx::smem_u32(s_tmem_slot), BN);
+      ptx::tmem_relinquish();
+    }
   }
   if (warp == kTmaWarp && lane == 0) ptx::tma_prefetch_desc(&tmap_w);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *s_tmem_slot;
+  // Barriers the gather warps and TMA copies report to: the leader's.
+  const uint32_t full_dst = PAIR ? ptx::mapa_shared(bar_full, 0) : bar_full;
+  const uint32_t wfull_dst = PAIR ? ptx::mapa_shared(bar_wfull, 0) : bar_wfull;
+  auto wait = [&](uint32_t bar, uint32_t parity, unsigned int site) -> bool {
+    return ptx::mbar_wait_bounded(bar, parity, s_abort, &g_bevk_watchdog, site);
+  };
 
   if (warp < kGatherWarps) {
     // ---------------------------------------------------------- geometry
@@ -290,10 +316,13 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
     };
     int cs = 0;          // stage slot of the stage being consumed
     uint32_t cph = 0;    // its phase
-    auto consume = [&](const Prefetch &P) -> bool {
-      if (!ptx::mbar_wait_bounded(bar_empty + 8 * cs, cph ^ 1, s_abort, &g_bevk_watchdog,
-                                  kSiteGatherEmpty))
-        return false;
+    auto consume = [&](Prefetch &P) -> bool {
+      // keep this stage's arithmetic behind the next stage's corner loads
+#pragma unroll
+      for (int i = 0; i < kRowsPerThread; ++i)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) ptx::reg_fence(P.v[i][q]);
+      if (!wait(bar_empty + 8 * cs, cph ^ 1, kSiteGatherEmpty)) return false;
       const uint32_t a_stage = sA + cs * L::kABytes;
 #pragma unroll
       for (int i = 0; i < kRowsPerThread; ++i) {
@@ -308,7 +337,10 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
       }
       ptx::fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_full + 8 * cs);
+      if (lane == 0) {
+        if constexpr (PAIR) ptx::mbar_arrive_cluster(full_dst + 8 * cs);
+        else ptx::mbar_arrive(bar_full + 8 * cs);
+      }
       if (++cs == STAGES) { cs = 0; cph ^= 1; }
       return true;
     };
@@ -330,7 +362,7 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
     }
 
     // ---------------------------------------------------------- epilogue
-    if (ok) ok = ptx::mbar_wait_bounded(bar_tmem, 0, s_abort, &g_bevk_watchdog, kSiteEpilogue);
+    if (ok) ok = wait(bar_tmem, 0, kSiteEpilogue);
     if (ok) {
       ptx::tc_fence_after();
       constexpr int kColsPerWarp = BN / 4;           // 4 warps share each TMEM lane quadrant
@@ -390,17 +422,26 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
       for (int kit = 0; kit < p.n_k; ++kit) {
         const int s = kit % STAGES;
         const uint32_t ph = (kit / STAGES) & 1;
-        if (!ptx::mbar_wait_bounded(bar_empty + 8 * s, ph ^ 1, s_abort, &g_bevk_watchdog,
-                                    kSiteTmaEmpty))
-          break;
+        if (!wait(bar_empty + 8 * s, ph ^ 1, kSiteTmaEmpty)) break;
         const int t = p.tap_major ? kit / p.n_cc : kit % p.T;
         const int cc = p.tap_major ? kit - (kit / p.n_cc) * p.n_cc : kit / p.T;
-        ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, L::kBBytes);
-        ptx::tma_load_2d(sB + s * L::kBBytes, &tmap_w, bar_wfull + 8 * s, t * p.Cin_pad + cc * kBK,
-                         n0);
+        if constexpr (PAIR) {
+          // the leader expects both CTAs' halves on its own barrier
+          if (leader) ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, 2 * L::kBBytes);
+          ptx::tma_load_2d_pair(sB + s * L::kBBytes, &tmap_w, wfull_dst + 8 * s,
+                                t * p.Cin_pad + cc * kBK, n0 + static_cast<int>(cr) * L::kBRows);
+        } else {
+          ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, L::kBBytes);
+          ptx::tma_load_2d(sB + s * L::kBBytes, &tmap_w, bar_wfull + 8 * s,
+                           t * p.Cin_pad + cc * kBK, n0);
+        }
         issued = kit + 1;
       }
-      if (*s_abort) {
+      if (*s_abort && PAIR) {
+        // Copies report to the leader's barrier; give this CTA's own copies
+        // time to land before its shared memory can be released.
+        for (int i = 0; i < 64; ++i) __nanosleep(2000);
+      } else if (*s_abort) {
         // Let this CTA's own copies land before its shared memory is released.
         volatile int never = 0;
         for (int kit = issued - STAGES < 0 ? 0 : issued - STAGES; kit < issued; ++kit)
@@ -408,31 +449,31 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
                                  &g_bevk_watchdog, kSiteTmaEmpty);
       }
     }
-  } else {  // MMA warp
-    if (lane == 0) {
-      constexpr uint32_t idesc = ptx::umma_idesc_f16(GM::kFmt, kBM, BN);
+  } else {  // MMA warp (the leader's, when paired)
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = ptx::umma_idesc_f16(GM::kFmt, PAIR ? 2 * kBM : kBM, BN);
       for (int kit = 0; kit < p.n_k; ++kit) {
         const int s = kit % STAGES;
         const uint32_t ph = (kit / STAGES) & 1;
-        if (!ptx::mbar_wait_bounded(bar_wfull + 8 * s, ph, s_abort, &g_bevk_watchdog,
-                                    kSiteMmaFull) ||
-            !ptx::mbar_wait_bounded(bar_full + 8 * s, ph, s_abort, &g_bevk_watchdog,
-                                    kSiteMmaFull))
+        if (!wait(bar_wfull + 8 * s, ph, kSiteMmaFull) || !wait(bar_full + 8 * s, ph, kSiteMmaFull))
           break;
         ptx::tc_fence_after();
         const uint32_t a_stage = sA + s * L::kABytes;
         const uint32_t b_stage = sB + s * L::kBBytes;
 #pragma unroll
         for (int k = 0; k < kBK / 16; ++k) {
-          ptx::umma_f16_ss(tmem_base, ptx::umma_desc_sw128(a_stage + k * 32),
-                           ptx::umma_desc_sw128(b_stage + k * 32), idesc,
-                           (kit | k) != 0 ? 1u : 0u);
+          const uint64_t ad = ptx::umma_desc_sw128(a_stage + k * 32);
+          const uint64_t bd = ptx::umma_desc_sw128(b_stage + k * 32);
+          if constexpr (PAIR) ptx::umma_f16_ss_pair(tmem_base, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
+          else ptx::umma_f16_ss(tmem_base, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
         }
-        ptx::umma_commit(bar_empty + 8 * s);
+        if constexpr (PAIR) ptx::umma_commit_pair_both(bar_empty + 8 * s, 0x3);
+        else ptx::umma_commit(bar_empty + 8 * s);
       }
       // Tracks completion of every MMA issued above (also on abort, so the
       // accumulator is quiescent before TMEM is released).
-      ptx::umma_commit(bar_tmem);
+      if constexpr (PAIR) ptx::umma_commit_pair_both(bar_tmem, 0x3);
+      else ptx::umma_commit(bar_tmem);
       if (*s_abort) {
         volatile int dummy = 0;
         ptx::mbar_wait_bounded(bar_tmem, 0, &dummy, &g_bevk_watchdog, kSiteEpilogue);
@@ -443,10 +484,31 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
 
   ptx::tc_fence_before();
   __syncthreads();
+  // Paired CTAs: neither leaves (or frees TMEM) while the other may still be
+  // reading its accumulator or arriving on its barriers.
+  if constexpr (PAIR) ptx::cluster_sync();
   if (warp == kMmaWarp) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, BN);
+    if constexpr (PAIR) ptx::tmem_dealloc_pair(tmem_base, BN);
+    else ptx::tmem_dealloc(tmem_base, BN);
   }
+}
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
+                  const T *__restrict__ x, const T *__restrict__ off, const T *__restrict__ msk,
+                  const T *__restrict__ bias, T *__restrict__ y) {
+  dcn_fwd_tc_body<T, BN, STAGES, false>(tmap_w, p, x, off, msk, bias, y);
+}
+
+template <typename T, int BN, int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+dcn_fwd_tc_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
+                       const T *__restrict__ x, const T *__restrict__ off,
+                       const T *__restrict__ msk, const T *__restrict__ bias,
+                       T *__restrict__ y) {
+  dcn_fwd_tc_body<T, BN, STAGES, true>(tmap_w, p, x, off, msk, bias, y);
 }
 
 // ---------------------------------------------------------------- host
@@ -470,12 +532,15 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, bool PAIR>
 int launch_tc(const TcParams &p, const CUtensorMap &tmap, const void *x, const void *off,
-              const void *msk, const void *bias, void *y, int tiles, cudaStream_t stream) {
-  using L = Smem<BN, STAGES>;
+              const void *msk, const void *bias, void *y, int ctas, cudaStream_t stream) {
+  using L = Smem<BN, STAGES, PAIR>;
   static_assert(L::kAlloc <= 232448, "shared memory budget");
-  auto kern = dcn_fwd_tc_kernel<T, BN, STAGES>;
+  auto kern = [] {
+    if constexpr (PAIR) return dcn_fwd_tc_pair_kernel<T, BN, STAGES>;
+    else return dcn_fwd_tc_kernel<T, BN, STAGES>;
+  }();
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -483,7 +548,7 @@ int launch_tc(const TcParams &p, const CUtensorMap &tmap, const void *x, const v
   });
   if (attr_err != cudaSuccess)
     return fail(BEVK_ERR_CUDA, "dcn tc: cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
-  kern<<<tiles, kThreads, L::kAlloc, stream>>>(tmap, p, static_cast<const T *>(x),
+  kern<<<ctas, kThreads, L::kAlloc, stream>>>(tmap, p, static_cast<const T *>(x),
                                                static_cast<const T *>(off),
                                                static_cast<const T *>(msk),
                                                static_cast<const T *>(bias), static_cast<T *>(y));
@@ -533,14 +598,18 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
     p.ms[i] = pr->mask_strides[i];
     p.ys[i] = pr->output_strides[i];
   }
-  const int64_t tiles = ((d.M + kBM - 1) / kBM) * p.n_tiles_n;
-  if (tiles > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn tc: too many tiles");
+  // Full-width tiles (BN = 256) run as CTA pairs: 256 pixels per cluster.
+  const bool pair = BN == 256;
+  const int64_t ctas = pair ? 2 * ((d.M + 2 * kBM - 1) / (2 * kBM)) * p.n_tiles_n
+                            : ((d.M + kBM - 1) / kBM) * p.n_tiles_n;
+  if (ctas > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn tc: too many tiles");
 
   CUtensorMap tmap;
   const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(d.T) * p.Cin_pad,
                               static_cast<cuuint64_t>(d.Cout)};
   const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(d.T) * p.Cin_pad * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(BN)};
+  // A paired CTA loads its half of the BN output channels per stage.
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(pair ? BN / 2 : BN)};
   const cuuint32_t estride[2] = {1, 1};
   const CUtensorMapDataType dt = pr->dtype == BEVK_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -549,17 +618,15 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return fail(BEVK_ERR_CUDA, "dcn tc: tensor map encode failed (%d)", int(cr));
 
-  const int nt = static_cast<int>(tiles);
-  // 3 stages: deep enough to overlap gather, TMA and MMA, small enough to leave
-  // ~60 KB of L1 for the corner lines (measured best among 2/3/4).
+  const int nc = static_cast<int>(ctas);
   if (pr->dtype == BEVK_DTYPE_F16) {
-    if (BN == 256) return launch_tc<__half, 256, 3>(p, tmap, x, off, msk, bias, y, nt, stream);
-    if (BN == 128) return launch_tc<__half, 128, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
-    return launch_tc<__half, 64, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
+    if (BN == 256) return launch_tc<__half, 256, 4, true>(p, tmap, x, off, msk, bias, y, nc, stream);
+    if (BN == 128) return launch_tc<__half, 128, 4, false>(p, tmap, x, off, msk, bias, y, nc, stream);
+    return launch_tc<__half, 64, 4, false>(p, tmap, x, off, msk, bias, y, nc, stream);
   }
-  if (BN == 256) return launch_tc<__nv_bfloat16, 256, 3>(p, tmap, x, off, msk, bias, y, nt, stream);
-  if (BN == 128) return launch_tc<__nv_bfloat16, 128, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
-  return launch_tc<__nv_bfloat16, 64, 4>(p, tmap, x, off, msk, bias, y, nt, stream);
+  if (BN == 256) return launch_tc<__nv_bfloat16, 256, 4, true>(p, tmap, x, off, msk, bias, y, nc, stream);
+  if (BN == 128) return launch_tc<__nv_bfloat16, 128, 4, false>(p, tmap, x, off, msk, bias, y, nc, stream);
+  return launch_tc<__nv_bfloat16, 64, 4, false>(p, tmap, x, off, msk, bias, y, nc, stream);
 }
 
 int read_and_clear_watchdog(int device, unsigned int *code) {

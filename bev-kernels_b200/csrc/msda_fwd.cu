@@ -7,23 +7,34 @@
 // with a sample dropped unless -1 < h < H_l and -1 < w < W_l and each of the
 // four corners zeroed outside [0, H_l-1] x [0, W_l-1].
 //
-// Design (C == 32, the BEVFormer head dim): one warp owns one (b, q, head)
-// unit.  Phase 1: lane s computes the geometry of sample s (up to 32 samples
-// per pass) -- level, corner indices, and the four corner weights with the
-// attention weight folded in -- and parks it in shared memory.  Phase 2: for
-// each sample the warp issues ONE load covering all four corners: lanes
-// 8g..8g+7 read corner g's 32-channel line (128 B for fp32) as 4-channel
-// vectors, so every load instruction moves four full lines.  Each lane keeps
-// a 4-channel partial sum for its corner slot; the four slots are folded with
-// two shuffles at the end.  No tensor cores: this is a gather, not a
-// contraction.  Any other C falls back to one thread per output element.
+// Design (C == 32, the BEVFormer head dim; L*P samples per (b, q, head) unit):
+// * Pass kernel (L*P = 4, 8, 16): a warp takes passes of 32 samples (32/(L*P)
+//   units).  Lane s computes the geometry of sample s -- four corner line
+//   indices and the four bilinear weights with the attention weight folded in
+//   -- into shared memory; the next pass's locations and weights are already
+//   being loaded.  Each sample then costs the warp ONE load instruction
+//   covering all four corners: lanes 8g..8g+7 read corner g's 32-channel line
+//   as 4-channel vectors, predicated (no branches), in batches.  Each lane
+//   keeps a 4-channel partial sum for its corner slot; the slots of a unit are
+//   folded with two shuffles when its last sample is done.  Passes are dealt
+//   round-robin over a grid of exactly the resident CTAs, so the grid walks
+//   the units in (batch, head, query) order together.
+// * Warp-per-unit kernel (other L*P): the same corner-slot mapping, one unit
+//   per warp, its samples in rounds of 32.
+// * Any other head dim: one thread per output element.
+// The gather is bound by the 16-byte loads a warp can keep in flight, which
+// the register file caps; batch sizes and CTAs per SM are the measured best.
+// No tensor cores: this is a gather, not a contraction.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cstdint>
 
 #include "bevk_internal.h"
+#include "bevk_ptx.cuh"
 
 namespace bevk {
 namespace {
@@ -179,6 +190,214 @@ msda_fwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ sha
   if (lane < 8) reinterpret_cast<VT *>(out + unit * C)[j] = V::from_f32(acc);
 }
 
+// Predicated vector loads of 4 channels (zeros when `pred` is 0).
+__device__ __forceinline__ uint4 ld_pred16(const void *p, uint32_t pred) {
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
+      "@q ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%5];\n\t}"
+      : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
+      : "r"(pred), "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 ld_pred8(const void *p, uint32_t pred) {
+  uint2 v = make_uint2(0u, 0u);
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+      "@q ld.global.nc.v2.u32 {%0, %1}, [%3];\n\t}"
+      : "+r"(v.x), "+r"(v.y)
+      : "r"(pred), "l"(p));
+  return v;
+}
+template <typename T>
+struct RawVec4;  // raw bits of 4 channels
+template <>
+struct RawVec4<float> {
+  using type = uint4;
+  __device__ static uint4 load(const void *p, uint32_t pred) { return ld_pred16(p, pred); }
+  __device__ static float4 f32(uint4 v) {
+    return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z),
+                       __uint_as_float(v.w));
+  }
+};
+template <>
+struct RawVec4<__half> {
+  using type = uint2;
+  __device__ static uint2 load(const void *p, uint32_t pred) { return ld_pred8(p, pred); }
+  __device__ static float4 f32(uint2 v) { return Vec4<__half>::to_f32(v); }
+};
+template <>
+struct RawVec4<__nv_bfloat16> {
+  using type = uint2;
+  __device__ static uint2 load(const void *p, uint32_t pred) { return ld_pred8(p, pred); }
+  __device__ static float4 f32(uint2 v) { return Vec4<__nv_bfloat16>::to_f32(v); }
+};
+
+struct CornerGeom {
+  int idx;   // line index (pixel * heads + head) relative to the camera's value base
+  float w;   // bilinear weight * attention weight; 0 for a dropped corner
+};
+constexpr int kPassWarps = 16;
+
+// LP = L*P samples per unit (a divisor of 32).  Loads go out in batches of
+// BATCH samples; with DB the next batch is issued before the current one is
+// consumed.  MINB is the number of CTAs per SM the register budget is cut for.
+template <typename T, int LP, int BATCH, bool DB, int MINB>
+__global__ void __launch_bounds__(kPassWarps * 32, MINB)
+msda_fwd_pass_kernel(const T *__restrict__ value, const int64_t *__restrict__ shapes,
+                     const int64_t *__restrict__ lsi, const T *__restrict__ loc,
+                     const T *__restrict__ attn, T *__restrict__ out, int S, int heads, int L,
+                     int Q, int P, int64_t passes) {
+  static_assert(32 % LP == 0, "LP must divide 32");
+  constexpr int C = 32;
+  constexpr int UPP = 32 / LP;  // units per pass
+  using R = RawVec4<T>;
+  using RT = typename R::type;
+  using V = Vec4<T>;
+  using VT = typename V::type;
+  __shared__ int s_lvl[kMaxLevels][3];
+  __shared__ CornerGeom s_geo[kPassWarps][32][4];
+  __shared__ int64_t s_vbase[kPassWarps][UPP];   // value element offset of the unit's camera
+  __shared__ int64_t s_obase[kPassWarps][UPP];   // output element offset of the unit
+
+  if (threadIdx.x < L) {
+    s_lvl[threadIdx.x][0] = static_cast<int>(shapes[2 * threadIdx.x]);
+    s_lvl[threadIdx.x][1] = static_cast<int>(shapes[2 * threadIdx.x + 1]);
+    s_lvl[threadIdx.x][2] = static_cast<int>(lsi[threadIdx.x]);
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 3;  // corner slot
+  const int j = lane & 7;   // 4-channel chunk of the head's 32 channels
+  // Passes are dealt round-robin to the warps of all CTAs, so the grid walks the
+  // units in (b, h, q) order together and the value lines in use at any moment
+  // are those of about one (camera, head) slice -- small enough to stay in L2
+  // even when the whole value tensor is not.
+  const int64_t p_stride = static_cast<int64_t>(gridDim.x) * kPassWarps;
+  const int64_t p_first = static_cast<int64_t>(blockIdx.x) * kPassWarps + warp;
+  const int64_t HQ = static_cast<int64_t>(heads) * Q;
+  const int my_l = (lane % LP) / P;  // level of this lane's sample (fixed across passes)
+
+  // unit v (in (b, h, q) order) of this lane's sample in pass `ps`
+  auto unit_of = [&](int64_t ps, int64_t &b, int &h, int64_t &q) {
+    const int64_t v = ps * UPP + lane / LP;
+    b = v / HQ;
+    const int64_t r = v - b * HQ;
+    h = static_cast<int>(r / Q);
+    q = r - static_cast<int64_t>(h) * Q;
+  };
+  // raw location / attention of this lane's sample in pass `ps`
+  auto fetch = [&](int64_t ps, float &lx, float &ly, float &a) {
+    int64_t b, q;
+    int h;
+    unit_of(ps, b, h, q);
+    const int64_t u = (b * Q + q) * heads + h;  // memory order (b, q, h)
+    const int i = lane % LP;
+    lx = to_f32(loc[(u * LP + i) * 2]);
+    ly = to_f32(loc[(u * LP + i) * 2 + 1]);
+    a = to_f32(attn[u * LP + i]);
+  };
+
+  float lx = 0.f, ly = 0.f, a = 0.f;
+  if (p_first < passes) fetch(p_first, lx, ly, a);
+  for (int64_t ps = p_first; ps < passes; ps += p_stride) {
+    // ---- geometry of this pass (lane = sample)
+    int64_t b, q;
+    int h;
+    unit_of(ps, b, h, q);
+    {
+      const int Hl = s_lvl[my_l][0], Wl = s_lvl[my_l][1], start = s_lvl[my_l][2];
+      CornerGeom cg[4] = {{0, 0.f}, {0, 0.f}, {0, 0.f}, {0, 0.f}};
+      const float h_im = ly * static_cast<float>(Hl) - 0.5f;
+      const float w_im = lx * static_cast<float>(Wl) - 0.5f;
+      if (h_im > -1.f && w_im > -1.f && h_im < static_cast<float>(Hl) &&
+          w_im < static_cast<float>(Wl)) {
+        const int h_low = static_cast<int>(floorf(h_im));
+        const int w_low = static_cast<int>(floorf(w_im));
+        const float lh = h_im - static_cast<float>(h_low);
+        const float lw = w_im - static_cast<float>(w_low);
+        const float hh = 1.f - lh, hw = 1.f - lw;
+        const bool y0 = h_low >= 0, y1 = h_low + 1 <= Hl - 1;
+        const bool x0 = w_low >= 0, x1 = w_low + 1 <= Wl - 1;
+        const int base = start + h_low * Wl + w_low;
+        if (y0 && x0) cg[0] = {base * heads + h, hh * hw * a};
+        if (y0 && x1) cg[1] = {(base + 1) * heads + h, hh * lw * a};
+        if (y1 && x0) cg[2] = {(base + Wl) * heads + h, lh * hw * a};
+        if (y1 && x1) cg[3] = {(base + Wl + 1) * heads + h, lh * lw * a};
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) s_geo[warp][lane][k] = cg[k];
+      if (lane % LP == 0) {
+        s_vbase[warp][lane / LP] = b * S * heads * C;
+        s_obase[warp][lane / LP] = ((b * Q + q) * heads + h) * C;
+      }
+    }
+    __syncwarp();
+    // next pass's raw inputs are loaded while this pass gathers
+    if (ps + p_stride < passes) fetch(ps + p_stride, lx, ly, a);
+
+    // ---- gather: batches of BATCH samples
+    RT buf[DB ? 2 : 1][BATCH];
+    float wbuf[DB ? 2 : 1][BATCH];
+    auto issue = [&](int bt, RT (&vb)[BATCH], float (&wb)[BATCH]) {
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k) {
+        const int smp = bt * BATCH + k;
+        const CornerGeom cgk = s_geo[warp][smp][g];
+        // camera of this sample's unit (units of a pass may straddle cameras)
+        const T *vb_ptr = value + s_vbase[warp][smp / LP] +
+                          static_cast<int64_t>(cgk.idx) * C + j * 4;
+        wb[k] = cgk.w;
+        vb[k] = R::load(vb_ptr, cgk.w != 0.f);
+      }
+    };
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto consume = [&](int bt, RT (&vb)[BATCH], float (&wb)[BATCH]) {
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k) {
+        ptx::reg_fence(vb[k]);
+        ptx::reg_fence(wb[k]);
+      }
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k) {
+        const int smp = bt * BATCH + k;
+        const float4 v = R::f32(vb[k]);
+        acc.x = fmaf(wb[k], v.x, acc.x);
+        acc.y = fmaf(wb[k], v.y, acc.y);
+        acc.z = fmaf(wb[k], v.z, acc.z);
+        acc.w = fmaf(wb[k], v.w, acc.w);
+        if ((smp + 1) % LP == 0) {  // last sample of a unit: fold corner slots, store
+#pragma unroll
+          for (int o = 8; o <= 16; o <<= 1) {
+            acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
+            acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
+            acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
+            acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
+          }
+          if (g == 0)
+            reinterpret_cast<VT *>(out + s_obase[warp][smp / LP])[j] = V::from_f32(acc);
+          acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    };
+    if constexpr (DB) {
+      issue(0, buf[0], wbuf[0]);
+#pragma unroll
+      for (int bt = 0; bt < 32 / BATCH; ++bt) {
+        if (bt + 1 < 32 / BATCH) issue(bt + 1, buf[(bt + 1) & 1], wbuf[(bt + 1) & 1]);
+        consume(bt, buf[bt & 1], wbuf[bt & 1]);
+      }
+    } else {
+#pragma unroll
+      for (int bt = 0; bt < 32 / BATCH; ++bt) {
+        issue(bt, buf[0], wbuf[0]);
+        consume(bt, buf[0], wbuf[0]);
+      }
+    }
+    __syncwarp();
+  }
+}
+
 // Any head dim: one thread per output element (b, q, m, c).
 template <typename T>
 __global__ void __launch_bounds__(256)
@@ -221,6 +440,33 @@ msda_fwd_generic_kernel(const T *__restrict__ value, const int64_t *__restrict__
   out[i] = from_f32<T>(acc);
 }
 
+// Resident CTAs per SM of one pass-kernel instantiation, computed once per
+// device; the grid is exactly that many CTAs per SM (the kernel loops).
+template <typename T, int LP, int BATCH, bool DB, int MINB>
+int launch_pass(const void *value, const int64_t *shapes, const int64_t *lsi, const void *loc,
+                const void *attn, int S, int heads, int L, int Q, int P, void *out,
+                int64_t passes, cudaStream_t stream) {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<int> resident[kMaxDevices];
+  const int dev = current_device();
+  const auto kern = msda_fwd_pass_kernel<T, LP, BATCH, DB, MINB>;
+  int per_sm = (dev >= 0 && dev < kMaxDevices) ? resident[dev].load(std::memory_order_relaxed) : 0;
+  if (per_sm <= 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPassWarps * 32, 0) !=
+            cudaSuccess ||
+        per_sm <= 0)
+      return fail(BEVK_ERR_CUDA, "msda: occupancy query failed");
+    if (dev >= 0 && dev < kMaxDevices) resident[dev].store(per_sm, std::memory_order_relaxed);
+  }
+  const int sms = device_info(dev).sm_count;
+  const int64_t ctas =
+      std::min<int64_t>(passes, static_cast<int64_t>(sms > 0 ? sms : 148) * per_sm);
+  kern<<<static_cast<unsigned>(ctas), kPassWarps * 32, 0, stream>>>(
+      static_cast<const T *>(value), shapes, lsi, static_cast<const T *>(loc),
+      static_cast<const T *>(attn), static_cast<T *>(out), S, heads, L, Q, P, passes);
+  return check_launch("msda_fwd_pass_kernel");
+}
+
 template <typename T>
 int launch_typed(const void *value, const int64_t *shapes, const int64_t *lsi, const void *loc,
                  const void *attn, int B, int S, int heads, int C, int L, int Q, int P,
@@ -230,6 +476,27 @@ int launch_typed(const void *value, const int64_t *shapes, const int64_t *lsi, c
   const size_t vec_bytes = sizeof(T) * 4;
   const bool fast = C == 32 && L <= kMaxLevels && aligned(value, vec_bytes) &&
                     aligned(out, vec_bytes);
+  const int LP = L * P;
+  // Batch sizes and CTAs per SM measured on B200 (1 level, P=4, Q=40000: 132 us
+  // with batches of 4 at 2 CTAs/SM against 158 us with double-buffered batches of
+  // 8 at 1 CTA/SM).  At L*P = 32 the warp-per-unit kernel is faster (499 us
+  // against 532 us on the 4-level, P=8 encoder workload), so it keeps that case.
+  if (fast && LP >= 4 && LP <= 16 && 32 % LP == 0 && units % (32 / LP) == 0) {
+    const int64_t passes = units / (32 / LP);
+    switch (LP) {
+      case 4:
+        return launch_pass<T, 4, 4, false, 2>(value, shapes, lsi, loc, attn, S, heads, L, Q, P,
+                                              out, passes, stream);
+      case 8:
+        return launch_pass<T, 8, 4, false, 2>(value, shapes, lsi, loc, attn, S, heads, L, Q, P,
+                                              out, passes, stream);
+      case 16:
+        return launch_pass<T, 16, 4, false, 3>(value, shapes, lsi, loc, attn, S, heads, L, Q,
+                                               P, out, passes, stream);
+      default:
+        break;
+    }
+  }
   if (fast) {
     const int64_t blocks = (units + kWarps - 1) / kWarps;
     if (blocks > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "msda: grid too large");

@@ -45,6 +45,9 @@ SMALL = [
     dict(B=1, shapes=[(9, 7), (5, 4)], M=4, C=32, Q=100, P=13),      # L*P > 32 samples
     dict(B=2, shapes=[(10, 12), (5, 6)], M=3, C=24, Q=50, P=3),      # generic kernel (C != 32)
     dict(B=1, shapes=[(1, 1), (2, 1)], M=8, C=32, Q=40, P=2),        # degenerate levels
+    dict(B=2, shapes=[(15, 17), (8, 9)], M=8, C=32, Q=123, P=4),     # L*P = 8 pass kernel
+    dict(B=1, shapes=[(13, 11), (7, 6), (4, 3), (2, 2)], M=8, C=32, Q=77, P=4),  # L*P = 16
+    dict(B=1, shapes=[(12, 10), (6, 5)], M=5, C=32, Q=33, P=2),      # units % 8 != 0
 ]
 
 
