@@ -91,7 +91,8 @@ def _out(n, pad, dil, k, stride):
 
 
 def dcn_work(cfg):
-    """Algorithmic FLOPs and unique bytes of one DCN forward (SURVEY 8(d) definitions)."""
+    """Algorithmic FLOPs and unique bytes of one DCN forward: 2*M*N*K FLOPs; input,
+    offset, mask, weight and output each read or written once."""
     B, C, H, W, Co = cfg["B"], cfg["C"], cfg["H"], cfg["W"], cfg["Cout"]
     Ho, Wo = _out(H, 1, 1, 3, 1), _out(W, 1, 1, 3, 1)
     flops = 2.0 * B * Ho * Wo * Co * C * 9

@@ -226,6 +226,30 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                : "memory");
 }
 
+// As umma_commit, arriving on the barrier at offset `bar` in every CTA of
+// `cta_mask` of the cluster.
+__device__ __forceinline__ void umma_commit_multicast(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// this CTA's shared memory to shared memory of a CTA of the cluster; the copy
+// completes its bytes as transactions on the mbarrier `bar` (a shared::cluster
+// address in the destination CTA).  Source data written with st.shared must be
+// ordered before the copy with fence_proxy_async_smem().
+__device__ __forceinline__ void bulk_copy_smem_to_cluster(uint32_t dst_cluster, uint32_t src_cta,
+                                                          uint32_t bytes, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+
 // Paired-CTA (cta_group::2) forms: TMEM allocation shared by the two CTAs of
 // a cluster (same warp in each CTA), M=256 MMA issued by the leader CTA, and
 // its completion signalled to the barrier at the same offset in both CTAs.
@@ -313,6 +337,37 @@ __device__ __forceinline__ uint4 ld_global_nc_v4_pred(const void *p, uint32_t pr
   return v;
 }
 
+// N 32-bit words held in registers (N = 4: 16 bytes, N = 8: 32 bytes).
+template <int N>
+struct Words {
+  uint32_t w[N];
+};
+
+// Unconditional read-only global vector load of 16 or 32 bytes (the address
+// must be aligned to the size).  The 32-byte form is the sm_100 256-bit load.
+template <int N>
+__device__ __forceinline__ Words<N> ld_global_nc_words(const void *p) {
+  Words<N> v;
+  if constexpr (N == 4) {
+    asm volatile("ld.global.nc.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+                 : "l"(p));
+  } else {
+    static_assert(N == 8, "16- or 32-byte loads");
+    asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]),
+                   "=r"(v.w[5]), "=r"(v.w[6]), "=r"(v.w[7])
+                 : "l"(p));
+  }
+  return v;
+}
+
+// As ld_global_nc_v4_pred, in the Words<4> form.
+__device__ __forceinline__ Words<4> ld_global_nc_words4_pred(const void *p, uint32_t pred) {
+  const uint4 v = ld_global_nc_v4_pred(p, pred);
+  return Words<4>{{v.x, v.y, v.z, v.w}};
+}
+
 // Scheduling fence on registers: no instruction is emitted, but code using
 // `v` afterwards cannot be hoisted above this point (nor above the volatile
 // loads issued before it).  Used to keep a prefetch ahead of the arithmetic
@@ -322,6 +377,11 @@ __device__ __forceinline__ void reg_fence(uint4 &v) {
 }
 __device__ __forceinline__ void reg_fence(uint2 &v) { asm volatile("" : "+r"(v.x), "+r"(v.y)); }
 __device__ __forceinline__ void reg_fence(float &v) { asm volatile("" : "+f"(v)); }
+template <int N>
+__device__ __forceinline__ void reg_fence(Words<N> &v) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(v.w[i]));
+}
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),

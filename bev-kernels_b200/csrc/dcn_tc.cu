@@ -45,11 +45,16 @@ namespace bevk {
 __device__ unsigned int g_bevk_watchdog = 0;
 
 namespace {
+// 128 bytes of zeros: corner reads that fall outside the image load from here
+// (never written; static device memory starts zeroed).
+__device__ __align__(128) uint32_t g_dcn_zero_line[32];
+}  // namespace
+
+namespace {
 
 constexpr int kBM = 128;           // pixels per tile (UMMA M)
 constexpr int kBK = 64;            // channels per stage (128 B of fp16/bf16)
 constexpr int kGatherWarps = 16;
-constexpr int kRowsPerThread = kBM / (kGatherWarps * 4);  // 8 lanes per row, 4 rows per warp pass
 constexpr int kThreads = (kGatherWarps + 2) * 32;
 constexpr int kTmaWarp = kGatherWarps;
 constexpr int kMmaWarp = kGatherWarps + 1;
@@ -72,6 +77,13 @@ struct TcParams {
   int64_t os[4], ms[4], ys[4];
 };
 
+// Tile schedules of the fused kernel.
+enum : int {
+  kModeSingle = 0,  // one CTA per 128-pixel x BN tile, M=128 MMA
+  kModePair = 1,    // 2-CTA cluster per 256-pixel x BN tile, M=256 cta_group::2 MMA
+  kModeNSplit = 2,  // 2-CTA cluster per 128-pixel x 2*BN tile, A rows shared
+};
+
 template <int BN, int STAGES, bool PAIR>
 struct Smem {
   // In a CTA pair each CTA holds half of the B tile (BN/2 output channels).
@@ -80,8 +92,8 @@ struct Smem {
   static constexpr int kBBytes = kBRows * kBK * 2;
   static constexpr int kA = 0;
   static constexpr int kB = kA + STAGES * kABytes;
-  static constexpr int kGW = kB + STAGES * kBBytes;          // uint4 weights [T][BM]
-  static constexpr int kGB = kGW + kMaxTaps * kBM * 16;      // int base offsets [T][BM]
+  static constexpr int kGW = kB + STAGES * kBBytes;          // 4 fp16 weights [T][BM]
+  static constexpr int kGB = kGW + kMaxTaps * kBM * 8;       // packed base + mask [T][BM]
   static constexpr int kBar = kGB + kMaxTaps * kBM * 4;      // full[S], wfull[S], empty[S], tmem_full
   static constexpr int kMisc = kBar + (3 * STAGES + 1) * 8;  // tmem slot, abort flag
   static constexpr int kTotal = kMisc + 16;
@@ -91,13 +103,17 @@ struct Smem {
 template <typename T>
 struct GatherMath;
 
+// Corner weights are kept in shared memory as four fp16 values (uint2:
+// corners 0,1 in .x, corners 2,3 in .y); prep() turns them into the operand
+// form of lerp2().
+
 // fp16: weights as half2 (w, w); packed half2 FMA chain.
 template <>
 struct GatherMath<__half> {
   static constexpr uint32_t kFmt = 0;
-  __device__ static uint32_t pack_weight(float w) {
-    __half2 h = __float2half2_rn(w);
-    return *reinterpret_cast<uint32_t *>(&h);
+  __device__ static uint4 prep(uint2 wh) {
+    return make_uint4(__byte_perm(wh.x, 0u, 0x1010), __byte_perm(wh.x, 0u, 0x3232),
+                      __byte_perm(wh.y, 0u, 0x1010), __byte_perm(wh.y, 0u, 0x3232));
   }
   __device__ static uint32_t lerp2(uint4 w, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     const __half2 r0 = __hmul2(*reinterpret_cast<const __half2 *>(&w.x),
@@ -120,7 +136,12 @@ struct GatherMath<__half> {
 template <>
 struct GatherMath<__nv_bfloat16> {
   static constexpr uint32_t kFmt = 1;
-  __device__ static uint32_t pack_weight(float w) { return __float_as_uint(w); }
+  __device__ static uint4 prep(uint2 wh) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&wh.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&wh.y));
+    return make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(b.x),
+                      __float_as_uint(b.y));
+  }
   __device__ static uint32_t lerp2(uint4 w, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     const float w0 = __uint_as_float(w.x), w1 = __uint_as_float(w.y);
     const float w2 = __uint_as_float(w.z), w3 = __uint_as_float(w.w);
@@ -150,14 +171,21 @@ __device__ __forceinline__ float ld_float<__nv_bfloat16>(const __nv_bfloat16 *p)
   return __bfloat162float(*p);
 }
 
-// Geometry of (tile row r, tap t): base element offset of corner (h_low, w_low)
-// and the four corner weights (mask folded in, 0 for dropped corners).
+__device__ __forceinline__ uint32_t half_bits(float w) {
+  return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(w)));
+}
+
+// Geometry of (tile row r, tap t).  `packed` = 2 * (element offset of corner
+// (h_low, w_low)) | (in-range bits of corners 0..3); the offset is a multiple
+// of 8 elements, so the low four bits are free and the offset comes back as
+// (packed >> 1) & ~7.  `wh` = the four corner weights (mask folded in, 0 for
+// dropped corners) in fp16.
 template <typename T>
 __device__ __forceinline__ void tap_geometry(const TcParams &p, const T *__restrict__ off,
-                                             const T *__restrict__ msk, int m, int t, int &base,
-                                             uint4 &wq) {
-  base = 0;
-  wq = make_uint4(0u, 0u, 0u, 0u);
+                                             const T *__restrict__ msk, int m, int t,
+                                             int &packed, uint2 &wh) {
+  packed = 0;
+  wh = make_uint2(0u, 0u);
   if (m >= p.M) return;
   const int HoWo = p.Ho * p.Wo;
   const int b = m / HoWo;
@@ -181,25 +209,42 @@ __device__ __forceinline__ void tap_geometry(const TcParams &p, const T *__restr
   const float hh = 1.f - lh, hw = 1.f - lw;
   const bool y0 = h_low >= 0, y1 = h_low + 1 <= p.H - 1;
   const bool x0 = w_low >= 0, x1 = w_low + 1 <= p.W - 1;
-  base = b * p.xs0 + h_low * p.xs2 + w_low * p.xs3;
-  wq.x = (y0 && x0) ? GatherMath<T>::pack_weight(hh * hw * mk) : 0u;
-  wq.y = (y0 && x1) ? GatherMath<T>::pack_weight(hh * lw * mk) : 0u;
-  wq.z = (y1 && x0) ? GatherMath<T>::pack_weight(lh * hw * mk) : 0u;
-  wq.w = (y1 && x1) ? GatherMath<T>::pack_weight(lh * lw * mk) : 0u;
+  const int base = b * p.xs0 + h_low * p.xs2 + w_low * p.xs3;
+  const int mask = (y0 && x0 ? 1 : 0) | (y0 && x1 ? 2 : 0) | (y1 && x0 ? 4 : 0) |
+                   (y1 && x1 ? 8 : 0);
+  packed = (base * 2) | mask;
+  const uint32_t w0 = (y0 && x0) ? half_bits(hh * hw * mk) : 0u;
+  const uint32_t w1 = (y0 && x1) ? half_bits(hh * lw * mk) : 0u;
+  const uint32_t w2 = (y1 && x0) ? half_bits(lh * hw * mk) : 0u;
+  const uint32_t w3 = (y1 && x1) ? half_bits(lh * lw * mk) : 0u;
+  wh = make_uint2(w0 | (w1 << 16), w2 | (w3 << 16));
 }
 
-// Kernel body.  PAIR = false: one CTA per 128-pixel tile, M=128 MMA.
-// PAIR = true: a 2-CTA cluster per 256-pixel tile; each CTA gathers its own
-// 128 pixels and TMA-loads half of the weight tile, the leader (rank 0) issues
-// M=256 tcgen05.mma.cta_group::2 reading both CTAs' operands, and each MMA
-// commit releases the stage in both CTAs.  Both CTAs' gather warps and TMA
-// copies report to the leader's barriers.
-template <typename T, int BN, int STAGES, bool PAIR>
+// Kernel body.
+// kModeSingle: one CTA per 128-pixel x BN tile, M=128 MMA.
+// kModePair: a 2-CTA cluster per 256-pixel x BN tile; each CTA gathers its own
+//   128 pixels and TMA-loads half of the weight tile, the leader (rank 0)
+//   issues M=256 tcgen05.mma.cta_group::2 reading both CTAs' operands, and
+//   each MMA commit releases the stage in both CTAs.  Both CTAs' gather warps
+//   and TMA copies report to the leader's barriers.
+// kModeNSplit: a 2-CTA cluster per 128-pixel x 2*BN tile; CTA c computes
+//   output channels [c*BN, c*BN+BN) of the same 128 pixels with its own M=128
+//   MMA.  Each CTA gathers only rows [c*64, c*64+64) of the A stage and a bulk
+//   copy puts them into the other CTA's A stage too, so every pixel is
+//   interpolated once for all 2*BN channels.  Each MMA commit is multicast to
+//   both CTAs' empty barriers: a stage is refilled only when both are done.
+template <typename T, int BN, int STAGES, int MODE, int VB>
 __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const TcParams &p,
                                                 const T *__restrict__ x,
                                                 const T *__restrict__ off,
                                                 const T *__restrict__ msk,
                                                 const T *__restrict__ bias, T *__restrict__ y) {
+  constexpr bool PAIR = MODE == kModePair;
+  constexpr bool NSPLIT = MODE == kModeNSplit;
+  constexpr bool CLUSTER = MODE != kModeSingle;
+  constexpr int kGRows = NSPLIT ? kBM / 2 : kBM;   // A rows this CTA gathers per stage
+  constexpr uint32_t kGBytes = kGRows * 128;       // their bytes in an A stage (copied
+                                                   // to the other CTA under NSPLIT)
   using L = Smem<BN, STAGES, PAIR>;
   using GM = GatherMath<T>;
   extern __shared__ uint8_t smem_raw[];
@@ -207,10 +252,12 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = ptx::smem_u32(smem);
   const uint32_t sA = sbase + L::kA, sB = sbase + L::kB;
-  uint4 *s_gw = reinterpret_cast<uint4 *>(smem + L::kGW);
+  uint2 *s_gw = reinterpret_cast<uint2 *>(smem + L::kGW);
   int *s_gb = reinterpret_cast<int *>(smem + L::kGB);
-  const uint32_t bar_full = sbase + L::kBar;            // A stage written (gather warps)
-  const uint32_t bar_wfull = bar_full + STAGES * 8;     // B stage landed (TMA bytes)
+  // full: A rows written by the gather warps (NSPLIT: this CTA's half).
+  // wfull: B stage landed (TMA bytes; NSPLIT: plus the other CTA's A half).
+  const uint32_t bar_full = sbase + L::kBar;
+  const uint32_t bar_wfull = bar_full + STAGES * 8;
   const uint32_t bar_empty = bar_wfull + STAGES * 8;    // stage consumed (tcgen05.commit)
   const uint32_t bar_tmem = bar_empty + STAGES * 8;
   uint32_t *s_tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kMisc);
@@ -218,27 +265,29 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t cr = PAIR ? ptx::cluster_ctarank() : 0u;   // rank in the CTA pair
+  const uint32_t cr = CLUSTER ? ptx::cluster_ctarank() : 0u;   // rank in the CTA pair
   const bool leader = cr == 0;
-  const int tile = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tile = CLUSTER ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int n_tile = tile % p.n_tiles_n;
-  const int m0 = (tile / p.n_tiles_n) * (PAIR ? 2 * kBM : kBM) + static_cast<int>(cr) * kBM;
-  const int n0 = n_tile * BN;
+  const int m_tile = tile / p.n_tiles_n;
+  const int m0 = PAIR ? m_tile * 2 * kBM + static_cast<int>(cr) * kBM : m_tile * kBM;
+  const int n0 = NSPLIT ? n_tile * 2 * BN + static_cast<int>(cr) * BN : n_tile * BN;
+  const int g_row0 = NSPLIT ? static_cast<int>(cr) * kGRows : 0;  // first tile row gathered here
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       // one arrive per gather warp (of both CTAs when paired)
       ptx::mbar_init(bar_full + 8 * s, PAIR ? 2 * kGatherWarps : kGatherWarps);
       ptx::mbar_init(bar_wfull + 8 * s, 1);                // TMA arrive + transaction bytes
-      ptx::mbar_init(bar_empty + 8 * s, 1);                // tcgen05.commit
+      ptx::mbar_init(bar_empty + 8 * s, NSPLIT ? 2 : 1);   // tcgen05.commit (of both CTAs)
     }
     ptx::mbar_init(bar_tmem, 1);
     *s_abort = 0;
     ptx::fence_mbar_init();
   }
-  // Paired CTAs: every barrier of both CTAs is initialised before any
+  // Clustered CTAs: every barrier of both CTAs is initialised before any
   // cross-CTA arrive or copy can target it.
-  if constexpr (PAIR) ptx::cluster_sync();
+  if constexpr (CLUSTER) ptx::cluster_sync();
   if (warp == kMmaWarp) {
     if constexpr (PAIR) {
       ptx::tmem_alloc_pair(ptx::smem_u32(s_tmem_slot), BN);
@@ -262,28 +311,42 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
 
   if (warp < kGatherWarps) {
     // ---------------------------------------------------------- geometry
-    for (int e = threadIdx.x; e < p.T * kBM; e += kGatherWarps * 32) {
-      const int t = e / kBM, r = e - (e / kBM) * kBM;
-      int base;
-      uint4 wq;
-      tap_geometry<T>(p, off, msk, m0 + r, t, base, wq);
-      s_gb[e] = base;
-      s_gw[e] = wq;
+    for (int e = threadIdx.x; e < p.T * kGRows; e += kGatherWarps * 32) {
+      const int t = e / kGRows, r = e - (e / kGRows) * kGRows;
+      int packed;
+      uint2 wh;
+      tap_geometry<T>(p, off, msk, m0 + g_row0 + r, t, packed, wh);
+      s_gb[e] = packed;
+      s_gw[e] = wh;
     }
     ptx::named_barrier_sync(1, kGatherWarps * 32);
 
     // ---------------------------------------------------------- gather
-    // Each thread owns kRowsPerThread rows x one 16-byte channel chunk of every
+    // Each lane owns one VB-byte vector (VB/2 channels) of a 128-byte tile
+    // row: kLanesPerRow lanes cover a row, one warp instruction covers
+    // kRowsPerInstr rows, and each thread owns kRowsPerThr rows of every
     // stage.  The four corner loads of all its rows for stage k+1 are issued
-    // (predicated, into registers) before stage k is interpolated and stored,
-    // so a full stage of corner reads is always in flight per thread.  Stage
-    // coordinates advance incrementally (no integer division in the loop).
-    const int j = lane & 7;     // 16-byte chunk (8 channels) within the 128-byte row
-    const int rsub = lane >> 3; // row within the warp's group of 4
+    // (into registers) before stage k is interpolated and stored, so a full
+    // stage of corner reads is always in flight per thread.  A corner outside
+    // the image reads the zero line instead, so every load is unconditional
+    // and exact (no weight-times-garbage).  Stage coordinates advance
+    // incrementally (no integer division in the loop).
+    constexpr int kLanesPerRow = 128 / VB;
+    constexpr int kRowsPerInstr = 32 / kLanesPerRow;
+    constexpr int kRowStride = kGatherWarps * kRowsPerInstr;  // between a thread's rows
+    constexpr int kRowsPerThr = kGRows / kRowStride;
+    static_assert(kRowsPerThr >= 1 && kGRows % kRowStride == 0, "gather lane layout");
+    constexpr int kWords = VB / 4;
+    using Vec = ptx::Words<kWords>;
+    const int j = lane % kLanesPerRow;
+    const int row0 = warp * kRowsPerInstr + lane / kLanesPerRow;
     const int xs2 = p.xs2, xs3 = p.xs3;
-    const int row0 = warp * 4 + rsub;          // rows row0 + i*kGatherWarps*4
+    const T *zline = reinterpret_cast<const T *>(g_dcn_zero_line) + j * (VB / 2);
+    // NSPLIT: the other CTA's A stages and B-full barriers
+    const uint32_t peer_sA = NSPLIT ? ptx::mapa_shared(sA, cr ^ 1u) : 0u;
+    const uint32_t peer_wfull = NSPLIT ? ptx::mapa_shared(bar_wfull, cr ^ 1u) : 0u;
     struct Prefetch {
-      uint4 v[kRowsPerThread][4];
+      Vec v[kRowsPerThr][4];
       int ebase;  // geometry index of the prefetched stage's first row
     };
     // (tap, channel chunk) of a stage index, advanced one stage at a time
@@ -299,19 +362,27 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
       return c;
     };
     auto issue = [&](StageCoord sc, Prefetch &P) {
-      const int c = sc.cc * kBK + j * 8;
-      const uint32_t cvalid = c < p.Cin ? 0xFFFFFFFFu : 0u;
-      const int ebase = sc.t * kBM + row0;
+      const int c = sc.cc * kBK + j * (VB / 2);
+      const int cvalid = c < p.Cin ? 0xF : 0;
+      const int ebase = sc.t * kGRows + row0;
       P.ebase = ebase;
 #pragma unroll
-      for (int i = 0; i < kRowsPerThread; ++i) {
-        const int e = ebase + i * (kGatherWarps * 4);
-        const uint4 wq = s_gw[e];
-        const int o = s_gb[e] + c;
-        P.v[i][0] = ptx::ld_global_nc_v4_pred(x + o, wq.x & cvalid);
-        P.v[i][1] = ptx::ld_global_nc_v4_pred(x + (o + xs3), wq.y & cvalid);
-        P.v[i][2] = ptx::ld_global_nc_v4_pred(x + (o + xs2), wq.z & cvalid);
-        P.v[i][3] = ptx::ld_global_nc_v4_pred(x + (o + xs2 + xs3), wq.w & cvalid);
+      for (int i = 0; i < kRowsPerThr; ++i) {
+        const int pk = s_gb[ebase + i * kRowStride];
+        const int mk = pk & cvalid;
+        const T *p0 = x + (((pk >> 1) & ~7) + c);
+        if constexpr (VB == 16) {
+          // 16-byte vectors: predicated loads (zeros when off)
+          P.v[i][0] = ptx::ld_global_nc_words4_pred(p0, mk & 1);
+          P.v[i][1] = ptx::ld_global_nc_words4_pred(p0 + xs3, mk & 2);
+          P.v[i][2] = ptx::ld_global_nc_words4_pred(p0 + xs2, mk & 4);
+          P.v[i][3] = ptx::ld_global_nc_words4_pred(p0 + (xs2 + xs3), mk & 8);
+        } else {
+          P.v[i][0] = ptx::ld_global_nc_words<kWords>((mk & 1) ? p0 : zline);
+          P.v[i][1] = ptx::ld_global_nc_words<kWords>((mk & 2) ? p0 + xs3 : zline);
+          P.v[i][2] = ptx::ld_global_nc_words<kWords>((mk & 4) ? p0 + xs2 : zline);
+          P.v[i][3] = ptx::ld_global_nc_words<kWords>((mk & 8) ? p0 + (xs2 + xs3) : zline);
+        }
       }
     };
     int cs = 0;          // stage slot of the stage being consumed
@@ -319,25 +390,42 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
     auto consume = [&](Prefetch &P) -> bool {
       // keep this stage's arithmetic behind the next stage's corner loads
 #pragma unroll
-      for (int i = 0; i < kRowsPerThread; ++i)
+      for (int i = 0; i < kRowsPerThr; ++i)
 #pragma unroll
         for (int q = 0; q < 4; ++q) ptx::reg_fence(P.v[i][q]);
       if (!wait(bar_empty + 8 * cs, cph ^ 1, kSiteGatherEmpty)) return false;
       const uint32_t a_stage = sA + cs * L::kABytes;
 #pragma unroll
-      for (int i = 0; i < kRowsPerThread; ++i) {
-        const int r = row0 + i * (kGatherWarps * 4);
-        const uint4 wq = s_gw[P.ebase + i * (kGatherWarps * 4)];
-        uint4 res;
-        res.x = GM::lerp2(wq, P.v[i][0].x, P.v[i][1].x, P.v[i][2].x, P.v[i][3].x);
-        res.y = GM::lerp2(wq, P.v[i][0].y, P.v[i][1].y, P.v[i][2].y, P.v[i][3].y);
-        res.z = GM::lerp2(wq, P.v[i][0].z, P.v[i][1].z, P.v[i][2].z, P.v[i][3].z);
-        res.w = GM::lerp2(wq, P.v[i][0].w, P.v[i][1].w, P.v[i][2].w, P.v[i][3].w);
-        ptx::st_shared_v4(a_stage + r * 128 + ((j ^ (r & 7)) << 4), res);
+      for (int i = 0; i < kRowsPerThr; ++i) {
+        const int r = g_row0 + row0 + i * kRowStride;  // row of the A tile
+        const uint4 wq = GM::prep(s_gw[P.ebase + i * kRowStride]);
+        uint32_t res[kWords];
+#pragma unroll
+        for (int w = 0; w < kWords; ++w)
+          res[w] = GM::lerp2(wq, P.v[i][0].w[w], P.v[i][1].w[w], P.v[i][2].w[w], P.v[i][3].w[w]);
+        // 16-byte chunks j*VB/16 .. of row r, at their 128-byte-swizzle slots
+#pragma unroll
+        for (int h = 0; h < VB / 16; ++h) {
+          const int chunk = j * (VB / 16) + h;
+          ptx::st_shared_v4(a_stage + r * 128 + ((chunk ^ (r & 7)) << 4),
+                            make_uint4(res[4 * h], res[4 * h + 1], res[4 * h + 2], res[4 * h + 3]));
+        }
       }
       ptx::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
+        if constexpr (NSPLIT) {
+          // This warp's rows (contiguous in the stage) also go to the other
+          // CTA's A stage, which is free: the empty barrier counts its MMA.
+#pragma unroll
+          for (int i = 0; i < kRowsPerThr; ++i) {
+            const uint32_t off_a = static_cast<uint32_t>(
+                (g_row0 + warp * kRowsPerInstr + i * kRowStride) * 128);
+            ptx::bulk_copy_smem_to_cluster(peer_sA + cs * L::kABytes + off_a,
+                                           a_stage + off_a, kRowsPerInstr * 128,
+                                           peer_wfull + 8 * cs);
+          }
+        }
         if constexpr (PAIR) ptx::mbar_arrive_cluster(full_dst + 8 * cs);
         else ptx::mbar_arrive(bar_full + 8 * cs);
       }
@@ -431,15 +519,16 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
           ptx::tma_load_2d_pair(sB + s * L::kBBytes, &tmap_w, wfull_dst + 8 * s,
                                 t * p.Cin_pad + cc * kBK, n0 + static_cast<int>(cr) * L::kBRows);
         } else {
-          ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, L::kBBytes);
+          // NSPLIT: the other CTA's A rows land on the same barrier
+          ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, L::kBBytes + (NSPLIT ? kGBytes : 0u));
           ptx::tma_load_2d(sB + s * L::kBBytes, &tmap_w, bar_wfull + 8 * s,
                            t * p.Cin_pad + cc * kBK, n0);
         }
         issued = kit + 1;
       }
-      if (*s_abort && PAIR) {
-        // Copies report to the leader's barrier; give this CTA's own copies
-        // time to land before its shared memory can be released.
+      if (*s_abort && CLUSTER) {
+        // Copies may report to the other CTA's barriers; give those issued
+        // here time to land before shared memory can be released.
         for (int i = 0; i < 64; ++i) __nanosleep(2000);
       } else if (*s_abort) {
         // Let this CTA's own copies land before its shared memory is released.
@@ -450,7 +539,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
       }
     }
   } else {  // MMA warp (the leader's, when paired)
-    if (lane == 0 && leader) {
+    if (lane == 0 && (leader || !PAIR)) {
       constexpr uint32_t idesc = ptx::umma_idesc_f16(GM::kFmt, PAIR ? 2 * kBM : kBM, BN);
       for (int kit = 0; kit < p.n_k; ++kit) {
         const int s = kit % STAGES;
@@ -468,6 +557,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
           else ptx::umma_f16_ss(tmem_base, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
         }
         if constexpr (PAIR) ptx::umma_commit_pair_both(bar_empty + 8 * s, 0x3);
+        else if constexpr (NSPLIT) ptx::umma_commit_multicast(bar_empty + 8 * s, 0x3);
         else ptx::umma_commit(bar_empty + 8 * s);
       }
       // Tracks completion of every MMA issued above (also on abort, so the
@@ -484,9 +574,9 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
 
   ptx::tc_fence_before();
   __syncthreads();
-  // Paired CTAs: neither leaves (or frees TMEM) while the other may still be
-  // reading its accumulator or arriving on its barriers.
-  if constexpr (PAIR) ptx::cluster_sync();
+  // Clustered CTAs: neither leaves (or frees TMEM) while the other may still
+  // be reading its accumulator, arriving on its barriers or copying into it.
+  if constexpr (CLUSTER) ptx::cluster_sync();
   if (warp == kMmaWarp) {
     ptx::tc_fence_after();
     if constexpr (PAIR) ptx::tmem_dealloc_pair(tmem_base, BN);
@@ -494,21 +584,31 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   }
 }
 
-template <typename T, int BN, int STAGES>
+// VB = bytes of input channels one gather lane loads per corner (16 or 32).
+template <typename T, int BN, int STAGES, int VB>
 __global__ void __launch_bounds__(kThreads, 1)
 dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
                   const T *__restrict__ x, const T *__restrict__ off, const T *__restrict__ msk,
                   const T *__restrict__ bias, T *__restrict__ y) {
-  dcn_fwd_tc_body<T, BN, STAGES, false>(tmap_w, p, x, off, msk, bias, y);
+  dcn_fwd_tc_body<T, BN, STAGES, kModeSingle, VB>(tmap_w, p, x, off, msk, bias, y);
 }
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, int VB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 dcn_fwd_tc_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
                        const T *__restrict__ x, const T *__restrict__ off,
                        const T *__restrict__ msk, const T *__restrict__ bias,
                        T *__restrict__ y) {
-  dcn_fwd_tc_body<T, BN, STAGES, true>(tmap_w, p, x, off, msk, bias, y);
+  dcn_fwd_tc_body<T, BN, STAGES, kModePair, VB>(tmap_w, p, x, off, msk, bias, y);
+}
+
+template <typename T, int BN, int STAGES, int VB>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+dcn_fwd_tc_nsplit_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
+                         const T *__restrict__ x, const T *__restrict__ off,
+                         const T *__restrict__ msk, const T *__restrict__ bias,
+                         T *__restrict__ y) {
+  dcn_fwd_tc_body<T, BN, STAGES, kModeNSplit, VB>(tmap_w, p, x, off, msk, bias, y);
 }
 
 // ---------------------------------------------------------------- host
@@ -532,22 +632,34 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <typename T, int BN, int STAGES, bool PAIR>
+template <typename T>
+struct TypeTag {
+  using type = T;
+};
+
+template <typename T, int BN, int STAGES, int MODE, int VB>
 int launch_tc(const TcParams &p, const CUtensorMap &tmap, const void *x, const void *off,
               const void *msk, const void *bias, void *y, int ctas, cudaStream_t stream) {
-  using L = Smem<BN, STAGES, PAIR>;
+  using L = Smem<BN, STAGES, MODE == kModePair>;
   static_assert(L::kAlloc <= 232448, "shared memory budget");
   auto kern = [] {
-    if constexpr (PAIR) return dcn_fwd_tc_pair_kernel<T, BN, STAGES>;
-    else return dcn_fwd_tc_kernel<T, BN, STAGES>;
+    if constexpr (MODE == kModePair) return dcn_fwd_tc_pair_kernel<T, BN, STAGES, VB>;
+    else if constexpr (MODE == kModeNSplit) return dcn_fwd_tc_nsplit_kernel<T, BN, STAGES, VB>;
+    else return dcn_fwd_tc_kernel<T, BN, STAGES, VB>;
   }();
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+  // the shared-memory opt-in is a per-device function attribute
+  constexpr int kMaxDevices = 64;
+  static std::once_flag once[kMaxDevices];
+  static cudaError_t attr_err[kMaxDevices];
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return fail(BEVK_ERR_CUDA, "dcn tc: bad device %d", dev);
+  std::call_once(once[dev], [&] {
+    attr_err[dev] =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   });
-  if (attr_err != cudaSuccess)
-    return fail(BEVK_ERR_CUDA, "dcn tc: cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+  if (attr_err[dev] != cudaSuccess)
+    return fail(BEVK_ERR_CUDA, "dcn tc: cudaFuncSetAttribute: %s",
+                cudaGetErrorString(attr_err[dev]));
   kern<<<ctas, kThreads, L::kAlloc, stream>>>(tmap, p, static_cast<const T *>(x),
                                                static_cast<const T *>(off),
                                                static_cast<const T *>(msk),
@@ -572,10 +684,10 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
                           const void *wpk, const void *bias, void *y, cudaStream_t stream) {
   if (xs[1] != 1 || xs[0] % 8 || xs[2] % 8 || xs[3] % 8 || !aligned(x, 16) || !aligned(wpk, 16))
     return fail(BEVK_ERR_MISALIGNED, "dcn tc: input must be channel-contiguous with 16-byte rows");
-  // int32 element offsets inside the kernel
   const int64_t extent = (d.B - 1) * xs[0] + (d.H - 1) * xs[2] + (d.W - 1) * xs[3] + d.Cin;
-  if (extent >= (int64_t(1) << 31) || xs[0] >= (int64_t(1) << 31))
-    return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn tc: input extent exceeds 32-bit indexing");
+  // int32 element offsets inside the kernel; corner offsets are stored doubled
+  if (extent >= (int64_t(1) << 30) || xs[0] >= (int64_t(1) << 30))
+    return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn tc: input extent exceeds 30-bit indexing");
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(BEVK_ERR_CUDA, "dcn tc: cuTensorMapEncodeTiled unavailable");
 
@@ -588,7 +700,12 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
   p.Cin_pad = d.Cin_g_pad;
   p.n_cc = p.Cin_pad / kBK;
   p.n_k = p.T * p.n_cc;
-  p.n_tiles_n = (d.Cout + BN - 1) / BN;
+  // Tile schedule: more than 256 output channels -> N-split CTA pairs (one
+  // gather per pixel for 512 channels); 129..256 -> M-paired CTAs (M=256
+  // MMA, half the weight tile per CTA); up to 128 -> single CTAs.
+  const int mode = d.Cout > 256 ? kModeNSplit : (BN == 256 ? kModePair : kModeSingle);
+  p.n_tiles_n = (d.Cout + (mode == kModeNSplit ? 2 * BN : BN) - 1) /
+                (mode == kModeNSplit ? 2 * BN : BN);
   p.tap_major = 0;
   p.mask_is_logit = pr->mask_is_logit;
   p.has_bias = pr->has_bias;
@@ -598,10 +715,9 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
     p.ms[i] = pr->mask_strides[i];
     p.ys[i] = pr->output_strides[i];
   }
-  // Full-width tiles (BN = 256) run as CTA pairs: 256 pixels per cluster.
-  const bool pair = BN == 256;
+  const bool pair = mode == kModePair;
   const int64_t ctas = pair ? 2 * ((d.M + 2 * kBM - 1) / (2 * kBM)) * p.n_tiles_n
-                            : ((d.M + kBM - 1) / kBM) * p.n_tiles_n;
+                            : (mode == kModeNSplit ? 2 : 1) * ((d.M + kBM - 1) / kBM) * p.n_tiles_n;
   if (ctas > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn tc: too many tiles");
 
   CUtensorMap tmap;
@@ -619,14 +735,26 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
   if (cr != CUDA_SUCCESS) return fail(BEVK_ERR_CUDA, "dcn tc: tensor map encode failed (%d)", int(cr));
 
   const int nc = static_cast<int>(ctas);
-  if (pr->dtype == BEVK_DTYPE_F16) {
-    if (BN == 256) return launch_tc<__half, 256, 4, true>(p, tmap, x, off, msk, bias, y, nc, stream);
-    if (BN == 128) return launch_tc<__half, 128, 4, false>(p, tmap, x, off, msk, bias, y, nc, stream);
-    return launch_tc<__half, 64, 4, false>(p, tmap, x, off, msk, bias, y, nc, stream);
-  }
-  if (BN == 256) return launch_tc<__nv_bfloat16, 256, 4, true>(p, tmap, x, off, msk, bias, y, nc, stream);
-  if (BN == 128) return launch_tc<__nv_bfloat16, 128, 4, false>(p, tmap, x, off, msk, bias, y, nc, stream);
-  return launch_tc<__nv_bfloat16, 64, 4, false>(p, tmap, x, off, msk, bias, y, nc, stream);
+  // 32-byte corner loads when every pixel row starts on a 32-byte boundary
+  // and a lane's 16 channels are all inside or all outside Cin (N-split CTAs
+  // gather 64 rows: one 16-byte vector per lane covers them).
+  const bool v32 = mode != kModeNSplit && d.Cin % 16 == 0 && xs[0] % 16 == 0 &&
+                   xs[2] % 16 == 0 && xs[3] % 16 == 0 && aligned(x, 32);
+  auto go = [&](auto tag) -> int {
+    using T = typename decltype(tag)::type;
+    if (mode == kModeNSplit)
+      return launch_tc<T, 256, 4, kModeNSplit, 16>(p, tmap, x, off, msk, bias, y, nc, stream);
+    if (v32) {
+      if (BN == 256) return launch_tc<T, 256, 4, kModePair, 32>(p, tmap, x, off, msk, bias, y, nc, stream);
+      if (BN == 128) return launch_tc<T, 128, 4, kModeSingle, 32>(p, tmap, x, off, msk, bias, y, nc, stream);
+      return launch_tc<T, 64, 4, kModeSingle, 32>(p, tmap, x, off, msk, bias, y, nc, stream);
+    }
+    if (BN == 256) return launch_tc<T, 256, 4, kModePair, 16>(p, tmap, x, off, msk, bias, y, nc, stream);
+    if (BN == 128) return launch_tc<T, 128, 4, kModeSingle, 16>(p, tmap, x, off, msk, bias, y, nc, stream);
+    return launch_tc<T, 64, 4, kModeSingle, 16>(p, tmap, x, off, msk, bias, y, nc, stream);
+  };
+  if (pr->dtype == BEVK_DTYPE_F16) return go(TypeTag<__half>{});
+  return go(TypeTag<__nv_bfloat16>{});
 }
 
 int read_and_clear_watchdog(int device, unsigned int *code) {

@@ -61,8 +61,8 @@ def test_dcn_columns_match_reference(path):
 
 
 def test_dcn_matches_torchvision():
-    """Third formulation: torchvision.ops.deform_conv2d (bit-identical to the
-    reference golden at config 1 in the survey probe)."""
+    """Third formulation: torchvision.ops.deform_conv2d, an independent
+    implementation of the same modulated deformable convolution."""
     tv = pytest.importorskip("torchvision")
     g = torch.Generator().manual_seed(3)
     x = torch.randn(2, 16, 11, 9, generator=g)
