@@ -71,7 +71,7 @@ enum : unsigned int {
 struct TcParams {
   int Cin, H, W, Ho, Wo, Cout, kW, T;
   int sh, sw, ph, pw, dh, dw;
-  int M, Cin_pad, n_cc, n_k, n_tiles_n, tap_major;
+  int M, Cin_pad, n_cc, n_k, n_tiles_n;
   int mask_is_logit, has_bias;
   int xs0, xs2, xs3;        // input strides (channel stride is 1)
   int64_t os[4], ms[4], ys[4];
@@ -270,6 +270,10 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   const int tile = CLUSTER ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int n_tile = tile % p.n_tiles_n;
   const int m_tile = tile / p.n_tiles_n;
+  // K order: stage kit covers tap kit % T of channel chunk kit / T.  Taps vary
+  // fastest, so the corner lines of one channel chunk are re-read from L1
+  // across consecutive stages.  (Starting each tile at a different K offset
+  // spreads the weight-tile reads over L2 but measured slower on B200.)
   const int m0 = PAIR ? m_tile * 2 * kBM + static_cast<int>(cr) * kBM : m_tile * kBM;
   const int n0 = NSPLIT ? n_tile * 2 * BN + static_cast<int>(cr) * BN : n_tile * BN;
   const int g_row0 = NSPLIT ? static_cast<int>(cr) * kGRows : 0;  // first tile row gathered here
@@ -354,10 +358,9 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
       int t, cc;
     };
     auto next_coord = [&](StageCoord c) {
-      if (p.tap_major) {
-        if (++c.cc == p.n_cc) { c.cc = 0; ++c.t; }
-      } else {
-        if (++c.t == p.T) { c.t = 0; ++c.cc; }
+      if (++c.t == p.T) {
+        c.t = 0;
+        ++c.cc;
       }
       return c;
     };
@@ -511,8 +514,8 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
         const int s = kit % STAGES;
         const uint32_t ph = (kit / STAGES) & 1;
         if (!wait(bar_empty + 8 * s, ph ^ 1, kSiteTmaEmpty)) break;
-        const int t = p.tap_major ? kit / p.n_cc : kit % p.T;
-        const int cc = p.tap_major ? kit - (kit / p.n_cc) * p.n_cc : kit / p.T;
+        const int t = kit % p.T;
+        const int cc = kit / p.T;
         if constexpr (PAIR) {
           // the leader expects both CTAs' halves on its own barrier
           if (leader) ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, 2 * L::kBBytes);
@@ -706,7 +709,6 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
   const int mode = d.Cout > 256 ? kModeNSplit : (BN == 256 ? kModePair : kModeSingle);
   p.n_tiles_n = (d.Cout + (mode == kModeNSplit ? 2 * BN : BN) - 1) /
                 (mode == kModeNSplit ? 2 * BN : BN);
-  p.tap_major = 0;
   p.mask_is_logit = pr->mask_is_logit;
   p.has_bias = pr->has_bias;
   p.xs0 = static_cast<int>(xs[0]); p.xs2 = static_cast<int>(xs[2]); p.xs3 = static_cast<int>(xs[3]);
@@ -742,8 +744,11 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
                    xs[2] % 16 == 0 && xs[3] % 16 == 0 && aligned(x, 32);
   auto go = [&](auto tag) -> int {
     using T = typename decltype(tag)::type;
+    // N-split CTAs hold the whole 256-channel weight tile per stage: three
+    // stages keep shared memory at 159 KB, leaving ~92 KB of L1 for the
+    // corner reads (four stages would leave ~28 KB and halve the hit rate).
     if (mode == kModeNSplit)
-      return launch_tc<T, 256, 4, kModeNSplit, 16>(p, tmap, x, off, msk, bias, y, nc, stream);
+      return launch_tc<T, 256, 3, kModeNSplit, 16>(p, tmap, x, off, msk, bias, y, nc, stream);
     if (v32) {
       if (BN == 256) return launch_tc<T, 256, 4, kModePair, 32>(p, tmap, x, off, msk, bias, y, nc, stream);
       if (BN == 128) return launch_tc<T, 128, 4, kModeSingle, 32>(p, tmap, x, off, msk, bias, y, nc, stream);
