@@ -287,7 +287,9 @@ def _max_over_ranks(v, dist):
     if dist is None:
         return v
     import torch
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    # NCCL reduces device tensors; gloo (CPU runs of the multi-rank logic) host ones
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
