@@ -42,6 +42,8 @@ EXPORTED_SYMBOLS = (
     "bevk_modulated_deformable_im2col_opt",
     "bevk_modulated_deformable_im2col_nhwc",
     "bevk_ms_deform_attn_forward",
+    "bevk_ms_deform_attn_backward_workspace_bytes",
+    "bevk_ms_deform_attn_backward",
 )
 
 
@@ -112,6 +114,11 @@ def lib():
     L.bevk_modulated_deformable_im2col_nhwc.argtypes = col_args + [i, vp, i, vp]
     L.bevk_ms_deform_attn_forward.restype = i
     L.bevk_ms_deform_attn_forward.argtypes = [vp, i64p, i64p, vp, vp] + [i] * 8 + [vp, i, vp]
+    L.bevk_ms_deform_attn_backward_workspace_bytes.restype = ctypes.c_size_t
+    L.bevk_ms_deform_attn_backward_workspace_bytes.argtypes = [i] * 5
+    L.bevk_ms_deform_attn_backward.restype = i
+    L.bevk_ms_deform_attn_backward.argtypes = ([vp, i64p, i64p, vp, vp, vp] + [i] * 8 +
+                                               [vp, vp, vp, vp, ctypes.c_size_t, i, vp])
     _lib = L
     return L
 

@@ -350,4 +350,41 @@ BEVK_API int bevk_ms_deform_attn_forward(const void *value, const int64_t *spati
                              reinterpret_cast<cudaStream_t>(stream));
 }
 
+BEVK_API size_t bevk_ms_deform_attn_backward_workspace_bytes(int batch, int spatial_size,
+                                                             int num_heads, int channels,
+                                                             int dtype) {
+  return msda_backward_workspace_bytes(batch, spatial_size, num_heads, channels, dtype);
+}
+
+BEVK_API int bevk_ms_deform_attn_backward(const void *value, const int64_t *spatial_shapes,
+                                          const int64_t *level_start_index,
+                                          const void *sampling_loc,
+                                          const void *attention_weights, const void *grad_output,
+                                          int batch, int spatial_size, int num_heads,
+                                          int channels, int num_levels, int num_query,
+                                          int num_point, int im2col_step, void *grad_value,
+                                          void *grad_sampling_loc, void *grad_attention_weights,
+                                          void *workspace, size_t workspace_bytes, int dtype,
+                                          bevk_stream_t stream) {
+  clear_error();
+  if (!value || !spatial_shapes || !level_start_index || !sampling_loc || !attention_weights ||
+      !grad_output || !grad_value || !grad_sampling_loc || !grad_attention_weights)
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "ms_deform_attn_backward: null pointer");
+  if (batch <= 0 || spatial_size <= 0 || num_heads <= 0 || channels <= 0 || num_levels <= 0 ||
+      num_query < 0 || num_point <= 0)
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "ms_deform_attn_backward: sizes must be positive");
+  if (im2col_step <= 0) return fail(BEVK_ERR_INVALID_ARGUMENT, "im2col_step must be positive");
+  const int step = batch < im2col_step ? batch : im2col_step;
+  if (batch % step != 0)
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "batch must divide im2col_step (batch=%d, step=%d)",
+                batch, step);
+  if (static_cast<int64_t>(spatial_size) * num_heads >= (int64_t(1) << 31) / 2)
+    return fail(BEVK_ERR_INDEX_OVERFLOW, "ms_deform_attn_backward: spatial_size*heads too large");
+  return launch_msda_backward(value, spatial_shapes, level_start_index, sampling_loc,
+                              attention_weights, grad_output, grad_value, grad_sampling_loc,
+                              grad_attention_weights, batch, spatial_size, num_heads, channels,
+                              num_levels, num_query, num_point, workspace, workspace_bytes, dtype,
+                              reinterpret_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -56,6 +56,12 @@ struct DcnDims {
 int dcn_dims(const bevk_dcn_problem *p, DcnDims *d);
 
 // Kernel launchers (return BEVK_OK or a status; arguments are pre-validated).
+size_t msda_backward_workspace_bytes(int B, int S, int heads, int C, int dtype);
+int launch_msda_backward(const void *value, const int64_t *shapes, const int64_t *lsi,
+                         const void *loc, const void *attn, const void *grad_out,
+                         void *grad_value, void *grad_loc, void *grad_attn, int B, int S,
+                         int heads, int C, int L, int Q, int P, void *workspace,
+                         size_t workspace_bytes, int dtype, cudaStream_t stream);
 int launch_msda_forward(const void *value, const int64_t *shapes, const int64_t *lsi,
                         const void *loc, const void *attn, int B, int S, int heads,
                         int C, int L, int Q, int P, void *out, int dtype,

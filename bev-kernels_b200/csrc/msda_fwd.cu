@@ -5,7 +5,10 @@
 //   out[b, q, m*C + c] = sum_{l,p} attn[b,q,m,l,p] * bilinear(value_l[b, :, m, c],
 //                        h = loc_y*H_l - 0.5, w = loc_x*W_l - 0.5)
 // with a sample dropped unless -1 < h < H_l and -1 < w < W_l and each of the
-// four corners zeroed outside [0, H_l-1] x [0, W_l-1].
+// four corners zeroed outside [0, H_l-1] x [0, W_l-1].  h and w are one fused
+// multiply-add each (__fmaf_rn), which is how nvcc compiles the reference's
+// `loc * H - 0.5f`; the bilinear derivative in the backward jumps at integer
+// coordinates, so the rounding of this expression is part of the contract.
 //
 // Design (C == 32, the BEVFormer head dim; L*P samples per (b, q, head) unit):
 // * Pass kernel (L*P = 4, 8, 16): a warp takes passes of 32 samples (32/(L*P)
@@ -145,8 +148,8 @@ msda_fwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ sha
       const float lx = to_f32(uloc[2 * s]);
       const float ly = to_f32(uloc[2 * s + 1]);
       const float a = to_f32(uattn[s]);
-      const float h_im = ly * static_cast<float>(Hl) - 0.5f;
-      const float w_im = lx * static_cast<float>(Wl) - 0.5f;
+      const float h_im = __fmaf_rn(ly, static_cast<float>(Hl), -0.5f);
+      const float w_im = __fmaf_rn(lx, static_cast<float>(Wl), -0.5f);
       if (h_im > -1.f && w_im > -1.f && h_im < static_cast<float>(Hl) &&
           w_im < static_cast<float>(Wl)) {
         const int h_low = static_cast<int>(floorf(h_im));
@@ -308,8 +311,8 @@ msda_fwd_pass_kernel(const T *__restrict__ value, const int64_t *__restrict__ sh
     {
       const int Hl = s_lvl[my_l][0], Wl = s_lvl[my_l][1], start = s_lvl[my_l][2];
       CornerGeom cg[4] = {{0, 0.f}, {0, 0.f}, {0, 0.f}, {0, 0.f}};
-      const float h_im = ly * static_cast<float>(Hl) - 0.5f;
-      const float w_im = lx * static_cast<float>(Wl) - 0.5f;
+      const float h_im = __fmaf_rn(ly, static_cast<float>(Hl), -0.5f);
+      const float w_im = __fmaf_rn(lx, static_cast<float>(Wl), -0.5f);
       if (h_im > -1.f && w_im > -1.f && h_im < static_cast<float>(Hl) &&
           w_im < static_cast<float>(Wl)) {
         const int h_low = static_cast<int>(floorf(h_im));
@@ -421,8 +424,8 @@ msda_fwd_generic_kernel(const T *__restrict__ value, const int64_t *__restrict__
     const int64_t ws = static_cast<int64_t>(heads) * C, hs = Wl * ws;
     for (int p = 0; p < P; ++p) {
       const int s = l * P + p;
-      const float h_im = to_f32(uloc[2 * s + 1]) * static_cast<float>(Hl) - 0.5f;
-      const float w_im = to_f32(uloc[2 * s]) * static_cast<float>(Wl) - 0.5f;
+      const float h_im = __fmaf_rn(to_f32(uloc[2 * s + 1]), static_cast<float>(Hl), -0.5f);
+      const float w_im = __fmaf_rn(to_f32(uloc[2 * s]), static_cast<float>(Wl), -0.5f);
       if (!(h_im > -1.f && w_im > -1.f && h_im < static_cast<float>(Hl) &&
             w_im < static_cast<float>(Wl)))
         continue;

@@ -1,16 +1,19 @@
-"""Multi-scale deformable attention (MSDA) forward for B200.
+"""Multi-scale deformable attention (MSDA) forward and backward for B200.
 
 Operator surface:
 * ``MultiScaleDeformableAttnFunction.apply(value, value_spatial_shapes,
   value_level_start_index, sampling_locations, attention_weights, im2col_step)``
   (the mmcv / BEVFormer convention);
 * ``ms_deform_attn_forward(value, spatial_shapes, level_start_index,
-  sampling_loc, attn_weight, *, im2col_step=64, force_generic=False)``
-  (msda_musa_opt2/msda_musa_opt2/dispatch.py:15-35 of the reference).
+  sampling_loc, attn_weight, *, im2col_step=64, force_generic=False)`` and
+  ``ms_deform_attn_backward(..., grad_output, *, im2col_step=64,
+  force_generic_col2im=False)`` (msda_musa_opt2/msda_musa_opt2/dispatch.py
+  :15-69 of the reference).
 
-Both run ``_ms_deform_attn_ext.forward`` -> ``bevk_ms_deform_attn_forward``:
-one warp per (batch, query, head), all four bilinear corners of a sample in
-one vector load, fp32 accumulation.  CUDA tensors only.
+They run ``_ms_deform_attn_ext.forward`` / ``.backward`` ->
+``bevk_ms_deform_attn_forward`` / ``_backward``: all four bilinear corners of
+a sample in one vector load, fp32 accumulation (fp32 atomics into grad_value
+in the backward).  CUDA tensors only.
 """
 from __future__ import annotations
 
@@ -42,6 +45,21 @@ def ms_deform_attn_forward(value: torch.Tensor, spatial_shapes: torch.Tensor,
                                force_generic=force_generic)
 
 
+def ms_deform_attn_backward(value: torch.Tensor, spatial_shapes: torch.Tensor,
+                            level_start_index: torch.Tensor, sampling_loc: torch.Tensor,
+                            attn_weight: torch.Tensor, grad_output: torch.Tensor, *,
+                            im2col_step: int = 64, force_generic_col2im: bool = False):
+    """-> (grad_value, grad_sampling_loc, grad_attn_weight), each in its
+    input's shape and dtype (dispatch.py:38-69 of the reference)."""
+    grad_value = torch.zeros_like(value)
+    grad_sampling_loc = torch.zeros_like(sampling_loc)
+    grad_attn_weight = torch.zeros_like(attn_weight)
+    _load_ext().backward(value, spatial_shapes, level_start_index, sampling_loc, attn_weight,
+                         grad_output, grad_value, grad_sampling_loc, grad_attn_weight,
+                         im2col_step=im2col_step, force_generic_col2im=force_generic_col2im)
+    return grad_value, grad_sampling_loc, grad_attn_weight
+
+
 class MultiScaleDeformableAttnFunction(Function):
     """autograd Function with the mmcv signature used by BEVFormer's
     TemporalSelfAttention / SpatialCrossAttention."""
@@ -60,12 +78,14 @@ class MultiScaleDeformableAttnFunction(Function):
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_output):
-        raise NotImplementedError(
-            "bev-kernels_b200: MultiScaleDeformableAttnFunction backward is not built yet "
-            "(forward-only release)")
+        value, shapes, level_start, loc, attn = ctx.saved_tensors
+        grad_value, grad_loc, grad_attn = ms_deform_attn_backward(
+            value, shapes, level_start, loc, attn, grad_output.contiguous(),
+            im2col_step=ctx.im2col_step)
+        return grad_value, None, None, grad_loc, grad_attn, None
 
 
 multi_scale_deformable_attn = MultiScaleDeformableAttnFunction.apply
 
-__all__ = ["ms_deform_attn_forward", "MultiScaleDeformableAttnFunction",
-           "multi_scale_deformable_attn"]
+__all__ = ["ms_deform_attn_forward", "ms_deform_attn_backward",
+           "MultiScaleDeformableAttnFunction", "multi_scale_deformable_attn"]

@@ -230,6 +230,43 @@ BEVK_API int bevk_ms_deform_attn_forward(
     int channels, int num_levels, int num_query, int num_point,
     int im2col_step, void *output, int dtype, bevk_stream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Multi-scale deformable attention, backward                               */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Bytes of device workspace bevk_ms_deform_attn_backward needs: 0 for f32;
+ * batch*spatial_size*num_heads*channels*4 for f16/bf16 (the fp32 grad_value
+ * accumulator, binding_musa.mu:450-507).
+ */
+BEVK_API size_t bevk_ms_deform_attn_backward_workspace_bytes(int batch, int spatial_size,
+                                                             int num_heads, int channels,
+                                                             int dtype);
+
+/*
+ * replaces _msda_opt2_musa.backward (csrc_musa/msda/binding_musa.mu:414-543,
+ * :550-556) / ms_deform_attn_backward (msda_musa_opt2/msda_musa_opt2/
+ * dispatch.py:38-69).  Same inputs as the forward plus grad_output
+ * [batch, num_query, num_heads*channels]; all contiguous, one dtype.
+ *   f32:      grad_value is ACCUMULATED into (the reference's callers pass
+ *             zeros); workspace may be NULL.
+ *   f16/bf16: grad_value is accumulated in the fp32 workspace (zeroed here)
+ *             and then written (narrowed) to grad_value.
+ * grad_sampling_loc [batch, num_query, num_heads, num_levels, num_point, 2]
+ * and grad_attention_weights [..., num_point] are written for every sample
+ * (zeros for samples outside the bilinear gate).  im2col_step as in the
+ * forward.  grad_value accumulation uses floating-point atomics, so its
+ * last bits vary from run to run, as in the reference.
+ */
+BEVK_API int bevk_ms_deform_attn_backward(
+    const void *value, const int64_t *spatial_shapes,
+    const int64_t *level_start_index, const void *sampling_loc,
+    const void *attention_weights, const void *grad_output, int batch,
+    int spatial_size, int num_heads, int channels, int num_levels,
+    int num_query, int num_point, int im2col_step, void *grad_value,
+    void *grad_sampling_loc, void *grad_attention_weights, void *workspace,
+    size_t workspace_bytes, int dtype, bevk_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -10,8 +10,9 @@ Parity status:
     fixtures in ``tests/golden`` (see ``tests/golden/make_golden.py``).
   * MSDA: parity unpinned by an executable reference (MUSA-only upstream, no
     golden vectors); restated from ``csrc_musa/msda/ms_deform_attn_kernels.cuh``
-    :7-49 and :559-623 and cross-checked against the independent grid_sample
-    formulation in ``oracle/msda_grid_sample.py``.
+    :7-49 and :559-623 (forward), :425-494 and :638-788 (backward) and
+    cross-checked against the independent grid_sample formulation in
+    ``oracle/msda_grid_sample.py`` (its torch autograd for the backward).
 
 All functions take and return numpy arrays (float32 compute; inputs of other
 float dtypes are up-cast, which is how fp16/bf16 kernel outputs are checked).
@@ -53,6 +54,9 @@ def _load():
         lib.oracle_msda_forward.restype = i
         lib.oracle_msda_forward.argtypes = (
             [_f32p, _i64p, _i64p, _f32p, _f32p] + [i] * 7 + [_f32p, i64, i64, i])
+        lib.oracle_msda_backward.restype = i
+        lib.oracle_msda_backward.argtypes = (
+            [_f32p, _i64p, _i64p, _f32p, _f32p, _f32p] + [i] * 7 + [_f32p] * 3 + [i])
         _lib = lib
     return _lib
 
@@ -151,6 +155,29 @@ def msda_forward(value, spatial_shapes, level_start_index, sampling_loc, attn_we
     if rc != 0:
         raise ValueError("oracle_msda_forward: invalid arguments")
     return out
+
+
+def msda_backward(value, spatial_shapes, level_start_index, sampling_loc, attn_weight,
+                  grad_output, nthreads=0):
+    """MSDA backward -> (grad_value [B,S,M,C], grad_loc [B,Q,M,L,P,2],
+    grad_attn [B,Q,M,L,P]) float32, grad_value starting from zero
+    (ms_deform_attn_kernels.cuh:425-494 / :638-788 semantics)."""
+    value, loc, attn = _f32(value), _f32(sampling_loc), _f32(attn_weight)
+    g = _f32(grad_output)
+    shapes = np.ascontiguousarray(np.asarray(spatial_shapes, dtype=np.int64))
+    lsi = np.ascontiguousarray(np.asarray(level_start_index, dtype=np.int64))
+    B, S, M, C = value.shape
+    _, Q, _, L, P, _ = loc.shape
+    gv = np.zeros(value.shape, np.float32)
+    gl = np.zeros(loc.shape, np.float32)
+    ga = np.zeros(attn.shape, np.float32)
+    rc = _load().oracle_msda_backward(_p(value), shapes.ctypes.data_as(_i64p),
+                                      lsi.ctypes.data_as(_i64p), _p(loc), _p(attn), _p(g),
+                                      B, S, M, C, L, Q, P, _p(gv), _p(gl), _p(ga),
+                                      int(nthreads))
+    if rc != 0:
+        raise ValueError("oracle_msda_backward: invalid arguments")
+    return gv, gl, ga
 
 
 def rel_l2(a, b) -> float:

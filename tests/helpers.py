@@ -95,6 +95,28 @@ def cabi_msda_forward(value, shapes, lsi, loc, attn, im2col_step=64):
     return out
 
 
+def cabi_msda_backward(value, shapes, lsi, loc, attn, grad_out, grad_value=None,
+                       im2col_step=64):
+    """Backward through the C ABI -> (grad_value, grad_loc, grad_attn); grad_value
+    starts from `grad_value` (f32 accumulates into it) or zeros."""
+    L = cabi.lib()
+    B, S, M, C = value.shape
+    _, Q, _, Lv, P, _ = loc.shape
+    gv = torch.zeros_like(value) if grad_value is None else grad_value
+    gl = torch.empty_like(loc)
+    ga = torch.empty_like(attn)
+    ws_bytes = L.bevk_ms_deform_attn_backward_workspace_bytes(B, S, M, C, DT[value.dtype])
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=value.device)
+    i64p = ctypes.POINTER(ctypes.c_int64)
+    cabi.check(L.bevk_ms_deform_attn_backward(
+        value.data_ptr(), ctypes.cast(shapes.data_ptr(), i64p), ctypes.cast(lsi.data_ptr(), i64p),
+        loc.data_ptr(), attn.data_ptr(), grad_out.data_ptr(), B, S, M, C, Lv, Q, P, im2col_step,
+        gv.data_ptr(), gl.data_ptr(), ga.data_ptr(), ws.data_ptr() if ws_bytes else None,
+        ws_bytes, DT[value.dtype], torch.cuda.current_stream().cuda_stream),
+        "msda_backward")
+    return gv, gl, ga
+
+
 def msda_inputs(seed, B, shapes, M, C, Q, P, oob_frac=0.02):
     """Seeded MSDA inputs with the BASELINE distributions (CPU fp32)."""
     g = torch.Generator().manual_seed(seed)

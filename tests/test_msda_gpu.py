@@ -1,4 +1,4 @@
-"""MSDA forward parity on the GPU (C ABI and Python surface) vs the CPU oracle.
+"""MSDA forward and backward parity on the GPU (C ABI and Python surface) vs the CPU oracle.
 
 Tolerances: fp32 within 1e-5 relative L2 and 1e-4 max-abs; fp16/bf16 within
 5e-3 relative L2 of the fp32 oracle on the up-cast inputs.
@@ -10,7 +10,8 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import (FP32_ABS, FP32_REL, HALF_REL, cabi_msda_forward, max_abs, msda_inputs,
+from helpers import (FP32_ABS, FP32_REL, HALF_REL, cabi_msda_backward, cabi_msda_forward,
+                     max_abs, msda_inputs,
                      rel_l2)
 from oracle import oracle
 
@@ -89,3 +90,79 @@ def test_im2col_step_contract(cuda):
     assert rel_l2(out, want) <= FP32_REL
     with pytest.raises(RuntimeError, match="contiguous"):
         ms_deform_attn.ms_deform_attn_forward(value.transpose(1, 2), shapes, lsi, loc, attn)
+
+
+# ------------------------------------------------------------------ backward
+def _oracle_bwd(value, shapes, lsi, loc, attn, gout):
+    return tuple(torch.from_numpy(a) for a in oracle.msda_backward(
+        value.float().cpu().numpy(), shapes.cpu().numpy(), lsi.cpu().numpy(),
+        loc.float().cpu().numpy(), attn.float().cpu().numpy(), gout.float().cpu().numpy()))
+
+
+def _bwd_case(cuda, cfg, dt, seed=7, oob=0.1):
+    value, shapes, lsi, loc, attn = msda_inputs(seed, oob_frac=oob, **cfg)
+    g = torch.Generator().manual_seed(seed + 1)
+    gout = torch.randn(cfg["B"], cfg["Q"], cfg["M"] * cfg["C"], generator=g)
+    value, loc, attn, gout = (t.to(cuda, dt) for t in (value, loc, attn, gout))
+    return value, shapes.to(cuda), lsi.to(cuda), loc, attn, gout
+
+
+def _check_grads(got, want, dt):
+    for name, a, b in zip(("grad_value", "grad_loc", "grad_attn"), got, want):
+        if dt == torch.float32:
+            assert rel_l2(a, b) <= FP32_REL, (name, rel_l2(a, b))
+            scale = float(b.abs().max()) or 1.0
+            assert max_abs(a, b) <= FP32_ABS * max(1.0, scale), (name, max_abs(a, b))
+        else:
+            assert a.dtype == dt and rel_l2(a, b) <= HALF_REL, (name, rel_l2(a, b))
+
+
+@pytest.mark.parametrize("cfg", SMALL, ids=[f"s{i}" for i in range(len(SMALL))])
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16],
+                         ids=["f32", "f16", "bf16"])
+def test_backward_small_cases(cuda, cfg, dt):
+    value, shapes, lsi, loc, attn, gout = _bwd_case(cuda, cfg, dt)
+    want = _oracle_bwd(value, shapes, lsi, loc, attn, gout)
+    _check_grads(cabi_msda_backward(value, shapes, lsi, loc, attn, gout), want, dt)
+
+
+@pytest.mark.parametrize("name", ["cfg4", "cfg5"])
+def test_backward_baseline_configs_full_size(cuda, name):
+    import ms_deform_attn
+    cfg = CFG4 if name == "cfg4" else CFG5
+    value, shapes, lsi, loc, attn, gout = _bwd_case(cuda, cfg, torch.float32, seed=2026,
+                                                    oob=0.02 if name == "cfg4" else 0.0)
+    want = _oracle_bwd(value, shapes, lsi, loc, attn, gout)
+    got = ms_deform_attn.ms_deform_attn_backward(value, shapes, lsi, loc, attn, gout)
+    _check_grads(got, want, torch.float32)
+
+
+def test_backward_through_autograd(cuda):
+    """MultiScaleDeformableAttnFunction.backward returns the op's gradients for
+    value, sampling_locations and attention_weights (and None for the rest)."""
+    import ms_deform_attn
+    cfg = SMALL[1]
+    value, shapes, lsi, loc, attn, gout = _bwd_case(cuda, cfg, torch.float32)
+    v, l, a = (t.clone().requires_grad_() for t in (value, loc, attn))
+    out = ms_deform_attn.MultiScaleDeformableAttnFunction.apply(v, shapes, lsi, l, a, 64)
+    out.backward(gout)
+    want = _oracle_bwd(value, shapes, lsi, loc, attn, gout)
+    _check_grads((v.grad, l.grad, a.grad), want, torch.float32)
+
+
+def test_backward_f32_accumulates_into_grad_value(cuda):
+    """fp32 grad_value is accumulated into (the reference's callers pass zeros)."""
+    cfg = SMALL[0]
+    value, shapes, lsi, loc, attn, gout = _bwd_case(cuda, cfg, torch.float32)
+    base = torch.randn_like(value)
+    gv, _, _ = cabi_msda_backward(value, shapes, lsi, loc, attn, gout, grad_value=base.clone())
+    want = _oracle_bwd(value, shapes, lsi, loc, attn, gout)[0]
+    assert rel_l2(gv - base, want) <= FP32_REL
+
+
+def test_backward_im2col_step_contract(cuda):
+    import ms_deform_attn
+    cfg = dict(SMALL[0], B=3)
+    value, shapes, lsi, loc, attn, gout = _bwd_case(cuda, cfg, torch.float32)
+    with pytest.raises(RuntimeError, match="im2col_step"):
+        ms_deform_attn.ms_deform_attn_backward(value, shapes, lsi, loc, attn, gout, im2col_step=2)

@@ -123,3 +123,38 @@ def test_msda_boundary_coordinates():
     attn = np.ones((1, 3, 1, 1, 1), np.float32)
     out = oracle.msda_forward(value, [[H, W]], [0], loc, attn)
     assert out[0, 0, 0] == 0 and out[0, 1, 0] == 0 and out[0, 2, 0] != 0
+
+
+def test_msda_backward_matches_autograd():
+    """Oracle backward (the reference's col2im formulas) against torch autograd
+    of the independent grid_sample formulation, in float64."""
+    g = torch.Generator().manual_seed(12)
+    shapes = [(11, 13), (6, 7), (3, 4)]
+    sizes = [h * w for h, w in shapes]
+    lsi = np.concatenate([[0], np.cumsum(sizes)[:-1]])
+    B, M, C, Q, L, P = 2, 3, 8, 40, 3, 4
+    value = torch.randn(B, sum(sizes), M, C, generator=g)
+    loc = torch.rand(B, Q, M, L, P, 2, generator=g) * 1.4 - 0.2      # some points outside
+    attn = torch.rand(B, Q, M, L, P, generator=g)
+    gout = torch.randn(B, Q, M * C, generator=g)
+    v64, l64, a64 = (t.double().requires_grad_() for t in (value, loc, attn))
+    out = msda_forward_grid_sample(v64, torch.tensor(shapes), l64, a64)
+    (out * gout.double()).sum().backward()
+    gv, gl, ga = oracle.msda_backward(value.numpy(), np.array(shapes), lsi, loc.numpy(),
+                                      attn.numpy(), gout.numpy())
+    for got, want in ((gv, v64.grad), (gl, l64.grad), (ga, a64.grad)):
+        want = want.numpy()
+        assert oracle.rel_l2(got, want) <= 1e-5, oracle.rel_l2(got, want)
+
+
+def test_msda_backward_zero_outside_gate():
+    """A sample outside the gate gets zero grad_loc / grad_attn and touches no
+    grad_value line (binding_musa.mu:414-543 writes zeros for it)."""
+    H, W = 4, 5
+    value = np.random.default_rng(0).standard_normal((1, H * W, 1, 2)).astype(np.float32)
+    loc = np.full((1, 1, 1, 1, 1, 2), 0.5, np.float32)
+    loc[..., 1] = -0.5 / H - 1e-3                       # h just below -1
+    attn = np.ones((1, 1, 1, 1, 1), np.float32)
+    gout = np.ones((1, 1, 2), np.float32)
+    gv, gl, ga = oracle.msda_backward(value, [[H, W]], [0], loc, attn, gout)
+    assert not gv.any() and not gl.any() and not ga.any()
