@@ -377,6 +377,43 @@ def bench_msda(cfg_name, steps, warmup, device, seed, stream):
     return dict(ms=ms, bytes=nbytes, per_launch_s=ms / 1e3 / steps, n_sets=len(sets))
 
 
+def msda_bwd_bytes(cfg):
+    """Algorithmic bytes of one MSDA backward: value, loc, attn and grad_out
+    read once; grad_value, grad_loc and grad_attn written once."""
+    B, M, C, Q, P = cfg["B"], cfg["M"], cfg["C"], cfg["Q"], cfg["P"]
+    L = len(cfg["shapes"])
+    S = sum(h * w for h, w in cfg["shapes"])
+    return 4 * (2 * B * S * M * C + 2 * (B * Q * M * L * P * 3) + B * Q * M * C)
+
+
+def bench_msda_bwd(cfg_name, steps, warmup, device, seed, stream):
+    """The backward op as a caller pays for it: grad_value zeroed (the
+    reference's wrapper allocates it with zeros_like) and the backward kernel."""
+    import torch
+    import _ms_deform_attn_ext as ext
+    cfg = MSDA_CFGS[cfg_name]
+    nbytes = msda_bwd_bytes(cfg)
+    sets = msda_sets(cfg, n_sets_for(nbytes, lo=2, hi=4), seed, device)
+    for i, s in enumerate(sets):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 131 + i)
+        B, Q, M, C = cfg["B"], cfg["Q"], cfg["M"], cfg["C"]
+        s["gout"] = torch.randn(B, Q, M * C, generator=g, device=device)
+        s["gv"] = torch.empty_like(s["value"])
+        s["gl"] = torch.empty_like(s["loc"])
+        s["ga"] = torch.empty_like(s["attn"])
+
+    def make(s):
+        def step():
+            s["gv"].zero_()
+            ext.backward(s["value"], s["shapes"], s["lsi"], s["loc"], s["attn"], s["gout"],
+                         s["gv"], s["gl"], s["ga"], 64, False)
+        return step
+
+    ms = graph_time([make(s) for s in sets], steps, warmup, stream)
+    return dict(ms=ms, bytes=nbytes, per_launch_s=ms / 1e3 / steps, n_sets=len(sets))
+
+
 # ----------------------------------------------------------------------------- CPU legs
 def cpu_dcn_sample(cfg_name, target_s, seed):
     """Time the CPU oracle on a bounded pixel range of the workload (all host threads).
@@ -456,7 +493,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--only", choices=("cfg2", "cfg3", "cfg4", "cfg5"),
+    ap.add_argument("--only", choices=("cfg2", "cfg3", "cfg4", "cfg5", "bwd_cfg4", "bwd_cfg5"),
                     help="time one workload's kernel only (profiling runs: no e2e, "
                          "secondary or CPU legs; prints a reduced line)")
     args = ap.parse_args()
@@ -490,6 +527,9 @@ def main():
             r = bench_dcn(args.only, args.steps, args.warmup, device, seed, 0, stream, dist)
             del r["sets"]
             extra = {"tflops": r["flops"] / r["per_launch_s"] / 1e12}
+        elif args.only.startswith("bwd_"):
+            r = bench_msda_bwd(args.only[4:], args.steps, args.warmup, device, seed, stream)
+            extra = {"algorithmic_GBps": r["bytes"] / r["per_launch_s"] / 1e9}
         else:
             r = bench_msda(args.only, args.steps, args.warmup, device, seed, stream)
             extra = {"algorithmic_GBps": r["bytes"] / r["per_launch_s"] / 1e9}
@@ -543,6 +583,17 @@ def main():
                 "algorithmic_GBps": gbs, "frac_hbm_peak": gbs / peaks["hbm_gbs"],
                 "roofline_us": r["bytes"] / (peaks["hbm_gbs"] * 1e9) * 1e6,
                 "traffic": _traffic(f"msda_fwd {name}")}
+            torch.cuda.empty_cache()
+        for name in ("cfg4", "cfg5"):
+            r = bench_msda_bwd(name, min(k2, 200), args.warmup, device, seed + 3, stream)
+            gbs = r["bytes"] / r["per_launch_s"] / 1e9
+            secondary[f"msda_bwd_{name}"] = {
+                "workload": MSDA_CFGS[name]["desc"].replace(" fwd", " bwd") +
+                            " (grad_value zeroing + backward kernel)",
+                "us_per_call": r["per_launch_s"] * 1e6,
+                "algorithmic_GBps": gbs, "frac_hbm_peak": gbs / peaks["hbm_gbs"],
+                "roofline_us": r["bytes"] / (peaks["hbm_gbs"] * 1e9) * 1e6,
+                "traffic": _traffic(f"msda_bwd {name}")}
             torch.cuda.empty_cache()
 
     cpu = None
