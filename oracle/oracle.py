@@ -6,8 +6,9 @@ plain-C restatement of the reference's algorithms).  Only ``tests/``,
 may import this module; the product package never does.
 
 Parity status:
-  * DCNv2: pinned against the reference's own PyTorch goldens through the
-    fixtures in ``tests/golden`` (see ``tests/golden/make_golden.py``).
+  * DCNv2 forward and backward: pinned against the reference's own PyTorch
+    goldens through the fixtures in ``tests/golden`` (see
+    ``tests/golden/make_golden.py``).
   * MSDA: parity unpinned by an executable reference (MUSA-only upstream, no
     golden vectors); restated from ``csrc_musa/msda/ms_deform_attn_kernels.cuh``
     :7-49 and :559-623 (forward), :425-494 and :638-788 (backward) and
@@ -54,6 +55,8 @@ def _load():
         lib.oracle_msda_forward.restype = i
         lib.oracle_msda_forward.argtypes = (
             [_f32p, _i64p, _i64p, _f32p, _f32p] + [i] * 7 + [_f32p, i64, i64, i])
+        lib.oracle_dcn_backward.restype = i
+        lib.oracle_dcn_backward.argtypes = [_f32p] * 5 + [i] * 15 + [_f32p] * 5 + [i]
         lib.oracle_msda_backward.restype = i
         lib.oracle_msda_backward.argtypes = (
             [_f32p, _i64p, _i64p, _f32p, _f32p, _f32p] + [i] * 7 + [_f32p] * 3 + [i])
@@ -136,6 +139,32 @@ def dcn_forward(x, offset, mask, weight, bias=None, stride=1, padding=0, dilatio
     if rc != 0:
         raise ValueError("oracle_dcn_forward: invalid arguments")
     return out
+
+
+def dcn_backward(x, offset, mask, weight, grad_out, stride=1, padding=0, dilation=1,
+                 groups=1, deform_groups=1, with_bias=True, nthreads=0):
+    """DCNv2 backward on NCHW arrays -> (grad_x, grad_offset, grad_mask,
+    grad_weight, grad_bias or None), float32 (modulated_deform_conv.py:269-312
+    / :405-499 semantics, double accumulation)."""
+    x, offset, mask, weight = _f32(x), _f32(offset), _f32(mask), _f32(weight)
+    go = _f32(grad_out)
+    B, C, H, W = x.shape
+    Cout, _, kH, kW = weight.shape
+    sh, sw = _pair(stride)
+    ph, pw = _pair(padding)
+    dh, dw = _pair(dilation)
+    gx = np.zeros(x.shape, np.float32)
+    goff = np.zeros(offset.shape, np.float32)
+    gm = np.zeros(mask.shape, np.float32)
+    gw = np.zeros(weight.shape, np.float32)
+    gb = np.zeros((Cout,), np.float32) if with_bias else None
+    rc = _load().oracle_dcn_backward(_p(x), _p(offset), _p(mask), _p(weight), _p(go),
+                                     B, C, H, W, Cout, kH, kW, sh, sw, ph, pw, dh, dw,
+                                     int(groups), int(deform_groups), _p(gx), _p(goff), _p(gm),
+                                     _p(gw), _p(gb) if gb is not None else None, int(nthreads))
+    if rc != 0:
+        raise ValueError("oracle_dcn_backward: invalid arguments")
+    return gx, goff, gm, gw, gb
 
 
 def msda_forward(value, spatial_shapes, level_start_index, sampling_loc, attn_weight,

@@ -12,7 +12,11 @@ modules by file path and records their outputs on small seeded inputs:
   (``modulated_deformable_im2col_pytorch``, NCHW columns) followed by the grouped
   ``mm`` + bias of ``ModulatedDeformConv2dFunction.forward`` (:380-401);
 * ``modulated_deform_conv/fused_tl.py:177-227`` (``dcn_columns_golden_nhwc`` /
-  ``dcn_forward_golden_nhwc``, NHWC, k = t*Cin + ci).
+  ``dcn_forward_golden_nhwc``, NHWC, k = t*Cin + ci);
+* the backward goldens ``modulated_deformable_col2im_pytorch`` and
+  ``modulated_deformable_col2im_coord_pytorch`` (:269-312: autograd through the
+  differentiable im2col golden) on the column gradient W^T . grad_out, and
+  grad_weight / grad_bias by autograd through the same golden forward.
 
 MSDA has no reference golden (the reference's MSDA exists only as MUSA kernels);
 ``msda_*.npz`` are produced by the independent grid_sample formulation in
@@ -99,6 +103,24 @@ def make_dcn(ref_mdc, ref_tl, out_dir):
         if b is not None:
             out = out + b.view(1, -1, 1, 1)
         arrays = dict(x=x, offset=off, mask=mask, weight=w, out=out)
+        # ---- backward goldens
+        gout = torch.randn(out.shape, generator=g)
+        dcol = torch.cat([wg[i].t() @ gout.permute(1, 0, 2, 3).reshape(groups, Cout // groups, -1)[i]
+                          for i in range(groups)], 0).view(C * kh * kw, B, Ho, Wo)
+        grad_x = ref_mdc.modulated_deformable_col2im_pytorch(
+            dcol, x, off, mask, kh, kw, pd[0], pd[1], st[0], st[1], dl[0], dl[1], dg)
+        grad_off, grad_mask = ref_mdc.modulated_deformable_col2im_coord_pytorch(
+            dcol, x, off, mask, kh, kw, pd[0], pd[1], st[0], st[1], dl[0], dl[1], dg)
+        w_var = w.detach().clone().requires_grad_(True)
+        cg_fwd = col2.detach().view(groups, -1, B * Ho * Wo)
+        out_w = torch.cat([w_var.view(groups, Cout // groups, -1)[i] @ cg_fwd[i]
+                           for i in range(groups)], 0)
+        (grad_w,) = torch.autograd.grad(out_w, [w_var], grad_outputs=gout.permute(
+            1, 0, 2, 3).reshape(Cout, B * Ho * Wo))
+        arrays.update(grad_out=gout, grad_x=grad_x, grad_offset=grad_off, grad_mask=grad_mask,
+                      grad_weight=grad_w)
+        if b is not None:
+            arrays["grad_bias"] = gout.sum(dim=(0, 2, 3))
         small = col2.numel() <= 200_000          # keep the fixture set small
         if small:
             arrays["columns_nchw"] = col2

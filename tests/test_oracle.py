@@ -158,3 +158,38 @@ def test_msda_backward_zero_outside_gate():
     gout = np.ones((1, 1, 2), np.float32)
     gv, gl, ga = oracle.msda_backward(value, [[H, W]], [0], loc, attn, gout)
     assert not gv.any() and not gl.any() and not ga.any()
+
+
+@pytest.mark.parametrize("path", DCN_FIXTURES, ids=lambda p: os.path.basename(p)[:-4])
+def test_dcn_backward_matches_reference_golden(path):
+    """Oracle backward against the reference's col2im / col2im_coord goldens
+    (autograd through its differentiable im2col) and autograd grad_weight."""
+    z = np.load(path)
+    k, st, pd, dl, groups, dg = _meta(z)
+    with_bias = "grad_bias" in z.files
+    gx, goff, gm, gw, gb = oracle.dcn_backward(z["x"], z["offset"], z["mask"], z["weight"],
+                                               z["grad_out"], st, pd, dl, groups, dg,
+                                               with_bias=with_bias)
+    for name, got in (("grad_x", gx), ("grad_offset", goff), ("grad_mask", gm),
+                      ("grad_weight", gw)) + ((("grad_bias", gb),) if with_bias else ()):
+        want = z[name]
+        assert oracle.rel_l2(got, want) <= 1e-5, (name, oracle.rel_l2(got, want))
+
+
+def test_dcn_backward_matches_torchvision_autograd():
+    """Third formulation: autograd of torchvision.ops.deform_conv2d."""
+    tv = pytest.importorskip("torchvision")
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(2, 8, 9, 10, generator=g, dtype=torch.float64)
+    w = torch.randn(12, 8, 3, 3, generator=g, dtype=torch.float64) * 0.2
+    off = torch.randn(2, 18, 9, 10, generator=g, dtype=torch.float64) * 1.5
+    mask = torch.sigmoid(torch.randn(2, 9, 9, 10, generator=g, dtype=torch.float64))
+    b = torch.randn(12, generator=g, dtype=torch.float64)
+    gout = torch.randn(2, 12, 9, 10, generator=g, dtype=torch.float64)
+    xs, ws, os_, ms, bs = (t.clone().requires_grad_() for t in (x, w, off, mask, b))
+    out = tv.ops.deform_conv2d(xs, os_, ws, bs, stride=1, padding=1, dilation=1, mask=ms)
+    out.backward(gout)
+    got = oracle.dcn_backward(x.float().numpy(), off.float().numpy(), mask.float().numpy(),
+                              w.float().numpy(), gout.float().numpy(), 1, 1, 1)
+    for a, t in zip(got, (xs, os_, ms, ws, bs)):
+        assert oracle.rel_l2(a, t.grad.numpy()) <= 2e-5, oracle.rel_l2(a, t.grad.numpy())
