@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "bevk_modulated_deformable_im2col",
     "bevk_modulated_deformable_im2col_opt",
     "bevk_modulated_deformable_im2col_nhwc",
+    "bevk_dcn_col2im",
     "bevk_ms_deform_attn_forward",
     "bevk_ms_deform_attn_backward_workspace_bytes",
     "bevk_ms_deform_attn_backward",
@@ -65,6 +66,19 @@ class DcnProblem(ctypes.Structure):
         ("output_strides", ctypes.c_int64 * 4),
         ("mask_is_logit", ctypes.c_int),
         ("has_bias", ctypes.c_int),
+    ]
+
+
+class DcnCol2imArgs(ctypes.Structure):
+    """Mirror of ``bevk_dcn_col2im_args``."""
+
+    _fields_ = [
+        ("problem", DcnProblem),
+        ("col_dtype", ctypes.c_int),
+        ("col_strides", ctypes.c_int64 * 3),
+        ("grad_input_strides", ctypes.c_int64 * 4),
+        ("grad_offset_strides", ctypes.c_int64 * 4),
+        ("grad_mask_strides", ctypes.c_int64 * 4),
     ]
 
 
@@ -105,6 +119,8 @@ def lib():
     L.bevk_dcn_forward.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp, sz, vp]
     L.bevk_dcn_forward_noalloc.restype = i
     L.bevk_dcn_forward_noalloc.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp]
+    L.bevk_dcn_col2im.restype = i
+    L.bevk_dcn_col2im.argtypes = [ctypes.POINTER(DcnCol2imArgs), vp, vp, vp, vp, vp, vp, vp, vp]
     col_args = [vp, vp, vp] + [i] * 15
     L.bevk_modulated_deformable_im2col.restype = i
     L.bevk_modulated_deformable_im2col.argtypes = col_args + [vp, i, vp]

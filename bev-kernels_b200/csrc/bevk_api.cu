@@ -350,6 +350,29 @@ BEVK_API int bevk_ms_deform_attn_forward(const void *value, const int64_t *spati
                              reinterpret_cast<cudaStream_t>(stream));
 }
 
+BEVK_API int bevk_dcn_col2im(const bevk_dcn_col2im_args *args, const void *input,
+                             const void *offset, const void *mask, const void *dcol,
+                             void *grad_input, void *grad_offset, void *grad_mask,
+                             bevk_stream_t stream) {
+  clear_error();
+  if (!args || !offset || !mask || !dcol)
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "dcn_col2im: null pointer");
+  if (!input && (grad_offset || grad_mask))
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "dcn_col2im: grad_offset / grad_mask need the input");
+  // out_channels and groups play no part in the scatter
+  bevk_dcn_problem pr = args->problem;
+  pr.out_channels = 1;
+  pr.groups = 1;
+  DcnDims d;
+  const int st = dcn_dims(&pr, &d);
+  if (st != BEVK_OK) return st;
+  if (args->col_dtype != args->problem.dtype && args->col_dtype != BEVK_DTYPE_F32)
+    return fail(BEVK_ERR_UNSUPPORTED, "dcn_col2im: column dtype must be the input dtype or f32");
+  if (!grad_input && !grad_offset && !grad_mask) return BEVK_OK;
+  return launch_dcn_col2im(args, d, input, offset, mask, dcol, grad_input, grad_offset,
+                           grad_mask, reinterpret_cast<cudaStream_t>(stream));
+}
+
 BEVK_API size_t bevk_ms_deform_attn_backward_workspace_bytes(int batch, int spatial_size,
                                                              int num_heads, int channels,
                                                              int dtype) {

@@ -56,6 +56,9 @@ struct DcnDims {
 int dcn_dims(const bevk_dcn_problem *p, DcnDims *d);
 
 // Kernel launchers (return BEVK_OK or a status; arguments are pre-validated).
+int launch_dcn_col2im(const bevk_dcn_col2im_args *a, const DcnDims &d, const void *input,
+                      const void *offset, const void *mask, const void *dcol, void *grad_input,
+                      void *grad_offset, void *grad_mask, cudaStream_t stream);
 size_t msda_backward_workspace_bytes(int B, int S, int heads, int C, int dtype);
 int launch_msda_backward(const void *value, const int64_t *shapes, const int64_t *lsi,
                          const void *loc, const void *attn, const void *grad_out,

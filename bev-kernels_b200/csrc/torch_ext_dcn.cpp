@@ -1,6 +1,7 @@
 // torch_ext_dcn.cpp -- module _modulated_deform_conv_ext: the reference
-// extension's forward op names (csrc/binding.cpp:142-191) over the C ABI, plus
-// the fused forward and weight packing used by modulated_deform_conv.
+// extension's op names (csrc/binding.cpp:142-191: im2col forward ops and the
+// col2im backward family) over the C ABI, plus the fused forward and weight
+// packing used by modulated_deform_conv.
 #include <cstring>
 
 #include "torch_ext_common.h"
@@ -195,6 +196,187 @@ void dcn_forward(const Tensor &input, const Tensor &offset, const Tensor &mask,
                "dcn_forward");
 }
 
+// ------------------------------------------------------------------ backward
+// Logical (b, c, h, w) strides of a tensor stored NCHW or NHWC ([B, H, W, C]).
+void logical_strides(const Tensor &t, bool nhwc, int64_t out[4]) {
+  if (nhwc) {
+    out[0] = t.stride(0); out[1] = t.stride(3); out[2] = t.stride(1); out[3] = t.stride(2);
+  } else {
+    for (int i = 0; i < 4; ++i) out[i] = t.stride(i);
+  }
+}
+
+// One gradient output of the scatter: written in place when it already is the
+// accumulation type and the op accumulates, else through an fp32 (fp64)
+// scratch that is added to it (accumulate) or copied over it (overwrite).
+struct GradOut {
+  Tensor *dst = nullptr;
+  Tensor buf;
+  bool overwrite = false;
+  void *prepare(at::ScalarType acc) {
+    if (dst == nullptr || !dst->defined()) return nullptr;
+    if (!overwrite && dst->scalar_type() == acc) return dst->data_ptr();
+    buf = at::zeros(dst->sizes(), dst->options().dtype(acc).memory_format(
+                                       dst->suggest_memory_format()));
+    return buf.data_ptr();
+  }
+  const Tensor &target() const { return buf.defined() ? buf : *dst; }
+  void finish() {
+    if (!buf.defined()) return;
+    if (overwrite) dst->copy_(buf);
+    else dst->add_(buf);
+  }
+};
+
+// col_nhwc: dcol is [M, kH*kW*C] (k = t*C + c) instead of [C*kH*kW, M];
+// img_nhwc: data_im [B, H, W, C], offset [B, Ho, Wo, 2T] or the fused
+// offset-conv output [B, Ho, Wo, 3T] (mask then read from it, pre-sigmoid),
+// mask [B, Ho, Wo, T], gradients in the same layouts.
+void col2im_common(const Tensor &dcol, const Tensor *data_im, const Tensor &offset,
+                   const Tensor &mask, int batch, int channels, int height, int width,
+                   int height_col, int width_col, int kernel_h, int kernel_w, int pad_h,
+                   int pad_w, int stride_h, int stride_w, int dil_h, int dil_w, int dg,
+                   bool col_nhwc, bool img_nhwc, Tensor *grad_im, Tensor *grad_offset,
+                   Tensor *grad_mask, bool overwrite_coord, const char *what) {
+  check_cuda(dcol, "dcol");
+  check_same_device(dcol, offset, "offset");
+  check_same_device(dcol, mask, "mask");
+  if (data_im) check_same_device(dcol, *data_im, "data_im");
+  TORCH_CHECK(dcol.is_contiguous(), "bevk: ", what, ": the column gradient must be contiguous");
+  const int T = kernel_h * kernel_w;
+  const int64_t M = static_cast<int64_t>(batch) * height_col * width_col;
+  TORCH_CHECK(dcol.numel() == static_cast<int64_t>(channels) * T * M, "bevk: ", what,
+              ": the column gradient has ", dcol.numel(), " elements, expected ",
+              static_cast<int64_t>(channels) * T * M);
+  const at::ScalarType xt = offset.scalar_type();
+  TORCH_CHECK(mask.scalar_type() == xt && (!data_im || data_im->scalar_type() == xt),
+              "bevk: ", what, ": data_im / offset / mask must share a dtype");
+  TORCH_CHECK(dcol.scalar_type() == xt || dcol.scalar_type() == at::kFloat, "bevk: ", what,
+              ": the column gradient must be float32 or the input dtype");
+  const bool fused_y = img_nhwc && offset.dim() == 4 && offset.size(-1) == 3 * T && dg == 1;
+  bevk_dcn_col2im_args a;
+  std::memset(&a, 0, sizeof(a));
+  bevk_dcn_problem &p = a.problem;
+  p.dtype = dtype_of(offset);
+  p.batch = batch; p.in_channels = channels; p.height = height; p.width = width;
+  p.out_channels = 1; p.kernel_h = kernel_h; p.kernel_w = kernel_w;
+  p.stride_h = stride_h; p.stride_w = stride_w; p.pad_h = pad_h; p.pad_w = pad_w;
+  p.dilation_h = dil_h; p.dilation_w = dil_w; p.groups = 1; p.deformable_groups = dg;
+  if (data_im) logical_strides(*data_im, img_nhwc, p.input_strides);
+  logical_strides(offset, img_nhwc, p.offset_strides);
+  const void *mask_ptr = mask.data_ptr();
+  if (fused_y) {
+    for (int i = 0; i < 4; ++i) p.mask_strides[i] = p.offset_strides[i];
+    mask_ptr = static_cast<const char *>(offset.data_ptr()) +
+               static_cast<int64_t>(2 * T) * offset.stride(3) * offset.element_size();
+    p.mask_is_logit = 1;
+  } else {
+    logical_strides(mask, img_nhwc, p.mask_strides);
+  }
+  a.col_dtype = dtype_of(dcol);
+  if (col_nhwc) {
+    a.col_strides[0] = static_cast<int64_t>(T) * channels; a.col_strides[1] = 1;
+    a.col_strides[2] = channels;
+  } else {
+    a.col_strides[0] = 1; a.col_strides[1] = static_cast<int64_t>(T) * M; a.col_strides[2] = M;
+  }
+  const at::ScalarType acc = xt == at::kDouble ? at::kDouble : at::kFloat;
+  GradOut gx, go, gm;
+  gx.dst = grad_im;
+  go.dst = grad_offset; go.overwrite = overwrite_coord;
+  gm.dst = grad_mask; gm.overwrite = overwrite_coord;
+  for (Tensor *t : {grad_im, grad_offset, grad_mask})
+    if (t && t->defined()) check_same_device(dcol, *t, "gradient");
+  const c10::cuda::CUDAGuard guard(dcol.device());
+  void *gx_ptr = gx.prepare(acc), *go_ptr = go.prepare(acc), *gm_ptr = gm.prepare(acc);
+  if (gx_ptr) logical_strides(gx.target(), img_nhwc, a.grad_input_strides);
+  if (go_ptr) logical_strides(go.target(), img_nhwc, a.grad_offset_strides);
+  if (gm_ptr) logical_strides(gm.target(), img_nhwc, a.grad_mask_strides);
+  check_status(bevk_dcn_col2im(&a, data_im ? data_im->data_ptr() : nullptr, offset.data_ptr(),
+                               mask_ptr, dcol.data_ptr(), gx_ptr, go_ptr, gm_ptr,
+                               current_stream(dcol)),
+               what);
+  gx.finish();
+  go.finish();
+  gm.finish();
+}
+
+#define BEVK_COL2IM_GEOM_ARGS                                                              \
+  int batch_size, int channels, int height_im, int width_im, int height_col, int width_col, \
+      int kernel_h, int kernel_w, int pad_h, int pad_w, int stride_h, int stride_w,          \
+      int dilation_h, int dilation_w, int deformable_group
+#define BEVK_COL2IM_GEOM                                                                   \
+  batch_size, channels, height_im, width_im, height_col, width_col, kernel_h, kernel_w,     \
+      pad_h, pad_w, stride_h, stride_w, dilation_h, dilation_w, deformable_group
+
+// csrc/binding.cpp:13-43: NCHW column matrix -> grad_im (accumulated)
+void col2im_nchw(const Tensor data_col, const Tensor data_offset, const Tensor data_mask,
+                 BEVK_COL2IM_GEOM_ARGS, Tensor grad_im) {
+  col2im_common(data_col, nullptr, data_offset, data_mask, BEVK_COL2IM_GEOM, false, false,
+                &grad_im, nullptr, nullptr, false, "modulated_deformable_col2im");
+}
+
+// csrc/binding.cpp:45-59: NCHW column matrix -> grad_offset, grad_mask (written)
+void col2im_coord_nchw(const Tensor data_col, const Tensor data_im, const Tensor data_offset,
+                       const Tensor data_mask, BEVK_COL2IM_GEOM_ARGS, Tensor grad_offset,
+                       Tensor grad_mask) {
+  col2im_common(data_col, &data_im, data_offset, data_mask, BEVK_COL2IM_GEOM, false, false,
+                nullptr, &grad_offset, &grad_mask, true, "modulated_deformable_col2im_coord");
+}
+
+// csrc/binding.cpp:80-87, :115-140: NHWC dcol -> grad_im, grad_offset, grad_mask
+// (accumulated into the caller's zeroed fp32 tensors)
+void col2im_nhwc(const Tensor dcol, const Tensor data_im, const Tensor data_offset,
+                 const Tensor data_mask, BEVK_COL2IM_GEOM_ARGS, Tensor grad_im,
+                 Tensor grad_offset, Tensor grad_mask) {
+  col2im_common(dcol, &data_im, data_offset, data_mask, BEVK_COL2IM_GEOM, true, true, &grad_im,
+                &grad_offset, &grad_mask, false, "modulated_deformable_col2im_nhwc");
+}
+
+// csrc/binding.cpp:89-95
+void col2im_coord_nhwc(const Tensor dcol, const Tensor data_im, const Tensor data_offset,
+                       const Tensor data_mask, BEVK_COL2IM_GEOM_ARGS, Tensor grad_offset,
+                       Tensor grad_mask) {
+  col2im_common(dcol, &data_im, data_offset, data_mask, BEVK_COL2IM_GEOM, true, true, nullptr,
+                &grad_offset, &grad_mask, false, "modulated_deformable_col2im_coord_nhwc");
+}
+
+// csrc/binding.cpp:97-113: NHWC dcol -> grad_im only
+void gradx_nhwc(const Tensor dcol, const Tensor data_offset, const Tensor data_mask,
+                BEVK_COL2IM_GEOM_ARGS, Tensor grad_im) {
+  col2im_common(dcol, nullptr, data_offset, data_mask, BEVK_COL2IM_GEOM, true, true, &grad_im,
+                nullptr, nullptr, false, "modulated_deformable_gradx_nhwc");
+}
+void gradx_gather_nhwc(const Tensor dcol, const Tensor data_offset, const Tensor data_mask,
+                       BEVK_COL2IM_GEOM_ARGS, int win, Tensor grad_im) {
+  (void)win;  // the reference's gather window; the scatter needs none
+  gradx_nhwc(dcol, data_offset, data_mask, BEVK_COL2IM_GEOM, grad_im);
+}
+
+// Generic scatter used by the autograd Functions: NCHW-shaped input / offset /
+// mask / gradients in any memory format, the column gradient [M, kH*kW*C]
+// (k = t*C + c); undefined gradient tensors are skipped.
+void dcn_col2im(const Tensor &dcol, const c10::optional<Tensor> &input, const Tensor &offset,
+                const Tensor &mask, int64_t in_channels, int64_t height, int64_t width,
+                int64_t kernel_h, int64_t kernel_w, int64_t stride_h, int64_t stride_w,
+                int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w,
+                int64_t deform_groups, c10::optional<Tensor> grad_input,
+                c10::optional<Tensor> grad_offset, c10::optional<Tensor> grad_mask) {
+  TORCH_CHECK(offset.dim() == 4 && mask.dim() == 4, "bevk: dcn_col2im: offset / mask must be 4-D");
+  Tensor gi = grad_input.has_value() ? *grad_input : Tensor();
+  Tensor go = grad_offset.has_value() ? *grad_offset : Tensor();
+  Tensor gm = grad_mask.has_value() ? *grad_mask : Tensor();
+  const Tensor *in = input.has_value() && input->defined() ? &*input : nullptr;
+  col2im_common(dcol, in, offset, mask, static_cast<int>(offset.size(0)),
+                static_cast<int>(in_channels), static_cast<int>(height), static_cast<int>(width),
+                static_cast<int>(offset.size(2)), static_cast<int>(offset.size(3)),
+                static_cast<int>(kernel_h), static_cast<int>(kernel_w), static_cast<int>(pad_h),
+                static_cast<int>(pad_w), static_cast<int>(stride_h), static_cast<int>(stride_w),
+                static_cast<int>(dil_h), static_cast<int>(dil_w), static_cast<int>(deform_groups),
+                true, false, gi.defined() ? &gi : nullptr, go.defined() ? &go : nullptr,
+                gm.defined() ? &gm : nullptr, false, "dcn_col2im");
+}
+
 int64_t watchdog(int64_t device) {
   unsigned int code = 0;
   bevk_device_watchdog(static_cast<int>(device), &code);
@@ -218,6 +400,34 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("stride_h"), py::arg("stride_w"), py::arg("pad_h"), py::arg("pad_w"),
         py::arg("dil_h"), py::arg("dil_w"), py::arg("groups"), py::arg("deform_groups"),
         py::arg("mask_is_logit") = false);
+  // backward column scatter under the reference's op names (csrc/binding.cpp:146-191)
+  for (const char *name : {"modulated_deformable_col2im_cuda", "modulated_deformable_col2im_opt_cuda",
+                           "modulated_deformable_col2im_smem_cuda"})
+    m.def(name, &col2im_nchw, "Column gradient [C*kH*kW, B*Ho*Wo] -> grad_im (accumulated)");
+  for (const char *name : {"modulated_deformable_col2im_coord_cuda",
+                           "modulated_deformable_col2im_coord_opt_cuda"})
+    m.def(name, &col2im_coord_nchw,
+          "Column gradient [C*kH*kW, B*Ho*Wo] -> grad_offset, grad_mask (written)");
+  for (const char *name : {"modulated_deformable_col2im_nhwc_cuda",
+                           "modulated_deformable_col2im_fused_smem_nhwc_cuda",
+                           "modulated_deformable_col2im_perelem_nhwc_cuda",
+                           "modulated_deformable_col2im_perelem_smem_nhwc_cuda"})
+    m.def(name, &col2im_nhwc,
+          "NHWC column gradient [M, kH*kW*C] -> grad_im, grad_offset, grad_mask (accumulated)");
+  m.def("modulated_deformable_col2im_coord_nhwc_cuda", &col2im_coord_nhwc,
+        "NHWC column gradient -> grad_offset, grad_mask (accumulated)");
+  m.def("modulated_deformable_gradx_smem_nhwc_cuda", &gradx_nhwc,
+        "NHWC column gradient -> grad_im (accumulated)");
+  m.def("modulated_deformable_gradx_gather_nhwc_cuda", &gradx_gather_nhwc,
+        "NHWC column gradient -> grad_im (accumulated)");
+  m.def("dcn_col2im", &dcn_col2im,
+        "DCN backward scatter: NHWC column gradient -> grad_input / grad_offset / grad_mask "
+        "(NCHW-shaped, any memory format, accumulated)",
+        py::arg("dcol"), py::arg("input"), py::arg("offset"), py::arg("mask"),
+        py::arg("in_channels"), py::arg("height"), py::arg("width"), py::arg("kernel_h"),
+        py::arg("kernel_w"), py::arg("stride_h"), py::arg("stride_w"), py::arg("pad_h"),
+        py::arg("pad_w"), py::arg("dil_h"), py::arg("dil_w"), py::arg("deform_groups"),
+        py::arg("grad_input"), py::arg("grad_offset"), py::arg("grad_mask"));
   m.def("watchdog", &watchdog, "Read and clear the device watchdog word (0 = clean)",
         py::arg("device"));
   m.def("version", []() { return bevk_version(); });

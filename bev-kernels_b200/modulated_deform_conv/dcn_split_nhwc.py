@@ -1,4 +1,5 @@
-"""NHWC DCNv2 entry points (the reference's default "fuse_c" backend surface,
+"""NHWC DCNv2 entry points, forward and backward (the reference's default
+"fuse_c" backend surface,
 ``modulated_deform_conv/dcn_split_nhwc.py``).
 
 Layouts follow the reference: x [B, H, W, Cin], offset-conv weight
@@ -89,16 +90,70 @@ class DCNSplitNHWCFunction(torch.autograd.Function):
                 bn_scale=None, bn_shift=None, act_relu=False):
         out, y = _forward_nhwc(x_nhwc, w_off, b_off, weight, bias, stride, padding, dilation,
                                bn_scale, bn_shift, act_relu)
-        ctx.save_for_backward(x_nhwc, y, w_off, weight)
         ctx.stride, ctx.padding, ctx.dilation = stride, padding, dilation
         ctx.with_bias = bias is not None
+        ctx.has_bn = bn_scale is not None
+        ctx.act_relu = bool(act_relu) and ctx.has_bn
+        saved = [x_nhwc, y, w_off, weight]
+        if ctx.has_bn:
+            saved.append(bn_scale)
+            if ctx.act_relu:
+                saved.append(out > 0)
+        ctx.save_for_backward(*saved)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        raise NotImplementedError(
-            "bev-kernels_b200: DCNSplitNHWCFunction backward is not built yet "
-            "(forward-only release)")
+        """dcn_split_nhwc.py:231-291: the BN scale and ReLU mask are folded into
+        dO; dCol = dO . W_flat^T (torch.mm); the scatter kernel reads offsets
+        and the pre-sigmoid mask straight from the offset-conv output y and
+        returns the mask gradient with the sigmoid backward applied;
+        grad_weight = Col^T . dO with Col re-gathered; the offset conv's own
+        backward is a regular convolution backward."""
+        import torch.nn.grad as tnng
+        ext = _load_ext()
+        saved = list(ctx.saved_tensors)
+        x, y, w_off, weight = saved[:4]
+        bn_scale = saved[4] if ctx.has_bn else None
+        relu_mask = saved[5] if ctx.act_relu else None
+        st, pd, dl = ctx.stride, ctx.padding, ctx.dilation
+        Cout, _, kH, kW = weight.shape
+        B, H, W, Cin = x.shape
+        T = kH * kW
+        Ho = out_size(H, pd, dl, kH, st)
+        Wo = out_size(W, pd, dl, kW, st)
+        M = B * Ho * Wo
+        K = T * Cin
+        dt = x.dtype
+        go = grad_out.reshape(M, Cout)
+        if ctx.has_bn:
+            if ctx.act_relu:
+                go = go * relu_mask.reshape(M, Cout)
+            go = go * bn_scale.to(go.dtype).view(1, -1)
+        dO = go.to(dt)
+        w_flat = weight.permute(2, 3, 1, 0).reshape(K, Cout).to(dt)      # [K, Cout], k = t*Cin + c
+        dcol = torch.mm(dO, w_flat.t())                                   # [M, K]
+        y_nhwc = y.permute(0, 2, 3, 1).contiguous()                       # [B, Ho, Wo, 3T]
+        gX = torch.zeros(B, H, W, Cin, device=x.device, dtype=torch.float32)
+        gOff = torch.zeros(B, Ho, Wo, 2 * T, device=x.device, dtype=torch.float32)
+        gMask = torch.zeros(B, Ho, Wo, T, device=x.device, dtype=torch.float32)
+        ext.modulated_deformable_col2im_nhwc_cuda(
+            dcol, x.contiguous(), y_nhwc, y_nhwc, B, Cin, H, W, Ho, Wo, kH, kW, pd, pd, st, st,
+            dl, dl, 1, gX, gOff, gMask)
+        cols = gather_cols_nhwc(x, y_nhwc, None, kH, kW, st, pd, dl)      # [M, K]
+        grad_weight = torch.mm(cols.t().float(), dO.float()) \
+            .view(kH, kW, Cin, Cout).permute(3, 2, 0, 1).contiguous().to(dt)
+        grad_bias = dO.float().sum(0).to(dt) if ctx.with_bias else None
+        # offset / mask convolution backward (regular convolution)
+        dY = torch.cat([gOff, gMask], dim=-1).permute(0, 3, 1, 2).contiguous()   # [B, 3T, Ho, Wo]
+        x_nchw = x.permute(0, 3, 1, 2).float()
+        w_off_f = w_off.float()
+        grad_x_off = tnng.conv2d_input(x_nchw.shape, w_off_f, dY, st, pd, dl)
+        grad_w_off = tnng.conv2d_weight(x_nchw, w_off_f.shape, dY, st, pd, dl)
+        grad_b_off = dY.sum(dim=(0, 2, 3))
+        grad_x = (gX + grad_x_off.permute(0, 2, 3, 1)).to(dt)
+        return (grad_x, grad_w_off.to(w_off.dtype), grad_b_off.to(w_off.dtype), grad_weight,
+                grad_bias, None, None, None, None, None, None)
 
 
 def dcn_split_nhwc(x_nhwc, w_off, b_off, weight, bias=None, stride=1, padding=1, dilation=1,

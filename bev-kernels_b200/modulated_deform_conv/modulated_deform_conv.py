@@ -162,9 +162,83 @@ class ModulatedDeformConv2dFunction(Function):
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_output):
-        raise NotImplementedError(
-            "bev-kernels_b200: ModulatedDeformConv2dFunction backward is not built yet "
-            "(forward-only release)")
+        input, offset, mask, weight, bias = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        grads = dcn_backward(input, offset, mask, weight, grad_output, ctx.stride, ctx.padding,
+                             ctx.dilation, ctx.groups, ctx.deform_groups,
+                             need_input=need[0], need_offset_mask=need[1] or need[2],
+                             need_weight=need[3], need_bias=ctx.with_bias and need[4])
+        return grads + (None, None, None, None, None)
+
+
+def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dilation,
+                 groups=1, deform_groups=1, need_input=True, need_offset_mask=True,
+                 need_weight=True, need_bias=True):
+    """Gradients of the DCNv2 forward (modulated_deform_conv.py:405-499) ->
+    (grad_input, grad_offset, grad_mask, grad_weight, grad_bias), None where
+    not requested.
+
+    The two contractions are plain GEMMs (cuBLAS through torch.mm, as in the
+    reference): the column gradient dcol = dO . W^T in pixel-major NHWC order
+    [M, kH*kW*C] (k = t*C + c), and grad_weight = dO^T . col with col from the
+    deformable im2col kernel.  The deformable part -- scatter of dcol into
+    grad_input and the offset / mask gradients -- is the bevk_dcn_col2im
+    kernel, which accumulates in fp32 (fp64 for fp64).
+    """
+    ext = _load_ext()
+    B, C, H, W = input.shape
+    Cout, Cg, kH, kW = weight.shape
+    T = kH * kW
+    sh, sw = _pair(stride)
+    ph, pw = _pair(padding)
+    dh, dw = _pair(dilation)
+    Ho = _out_size(H, ph, dh, kH, sh)
+    Wo = _out_size(W, pw, dw, kW, sw)
+    M = B * Ho * Wo
+    G = groups
+    Coutg = Cout // G
+    dt = input.dtype
+    acc = torch.float64 if dt == torch.float64 else torch.float32
+    go = grad_output.to(dt).permute(0, 2, 3, 1).reshape(M, Cout)    # [M, Cout]
+
+    grad_input = grad_offset = grad_mask = grad_weight = grad_bias = None
+    if need_input or need_offset_mask:
+        # dcol[m, t*C + c] = sum_co dO[m, co] * weight[co, c_local, t]  (per conv group)
+        wt = weight.to(dt).permute(0, 2, 3, 1).reshape(G, Coutg, T * Cg)   # k = t*Cg + c
+        if G == 1:
+            dcol = torch.mm(go, wt[0])
+        else:
+            dcol = torch.stack([torch.mm(go[:, g * Coutg:(g + 1) * Coutg], wt[g])
+                                for g in range(G)], 1)                      # [M, G, T*Cg]
+            dcol = dcol.view(M, G, T, Cg).permute(0, 2, 1, 3).reshape(M, T * C)
+        fmt = (torch.channels_last if input.is_contiguous(memory_format=torch.channels_last)
+               else torch.contiguous_format)
+        gx = (torch.zeros(B, C, H, W, device=input.device, dtype=acc).contiguous(
+            memory_format=fmt) if need_input else None)
+        goff = torch.zeros(offset.shape, device=input.device, dtype=acc) if need_offset_mask else None
+        gmsk = torch.zeros(mask.shape, device=input.device, dtype=acc) if need_offset_mask else None
+        ext.dcn_col2im(dcol, input if need_offset_mask else None, offset, mask, C, H, W, kH, kW,
+                       sh, sw, ph, pw, dh, dw, deform_groups, gx, goff, gmsk)
+        if need_input:
+            grad_input = gx.to(dt)
+        if need_offset_mask:
+            grad_offset = goff.to(offset.dtype)
+            grad_mask = gmsk.to(mask.dtype)
+    if need_weight:
+        # reference column matrix [C*T, M] (k = c*T + t) from the im2col kernel
+        col = input.new_empty(C * T, M)
+        ext.modulated_deformable_im2col_opt_cuda(
+            input.contiguous(), offset.contiguous(), mask.contiguous(), B, C, H, W, Ho, Wo,
+            kH, kW, ph, pw, sh, sw, dh, dw, deform_groups, col)
+        if G == 1:
+            gw = torch.mm(go.t(), col.t())
+        else:
+            gw = torch.cat([torch.mm(go[:, g * Coutg:(g + 1) * Coutg].t(),
+                                     col[g * Cg * T:(g + 1) * Cg * T].t()) for g in range(G)], 0)
+        grad_weight = gw.view_as(weight).to(weight.dtype)
+    if need_bias:
+        grad_bias = go.to(acc).sum(0).to(dt)
+    return grad_input, grad_offset, grad_mask, grad_weight, grad_bias
 
 
 modulated_deform_conv2d = ModulatedDeformConv2dFunction.apply

@@ -209,6 +209,53 @@ BEVK_API int bevk_modulated_deformable_im2col_nhwc(
     bevk_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* DCNv2 backward: column scatter                                           */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Arguments of bevk_dcn_col2im.  `problem` gives the geometry, the input /
+ * offset / mask dtype and strides and mask_is_logit (out_channels, groups,
+ * output_strides and has_bias are not used).  The column gradient dcol holds
+ * element (pixel m, input channel c, tap t) at
+ *   dcol[m*col_strides[0] + c*col_strides[1] + t*col_strides[2]],
+ * m = (b*Ho + oh)*Wo + ow, t = ki*kW + kj; its dtype is the problem dtype or
+ * BEVK_DTYPE_F32.  The reference's NCHW column matrix [C*kH*kW, B*Ho*Wo]
+ * (modulated_deform_conv.py:444-451) has col_strides {1, kH*kW*M, M}; the NHWC
+ * matrix [M, kH*kW*C] of dcn_split_nhwc.py:200 has {kH*kW*C, 1, C}.  Gradient
+ * strides are element strides (b, channel, h, w) of the fp32 gradient
+ * buffers (fp64 for fp64 problems).
+ */
+typedef struct bevk_dcn_col2im_args {
+  bevk_dcn_problem problem;
+  int col_dtype;
+  int64_t col_strides[3];
+  int64_t grad_input_strides[4];
+  int64_t grad_offset_strides[4];
+  int64_t grad_mask_strides[4];
+} bevk_dcn_col2im_args;
+
+/*
+ * replaces modulated_deformable_col2im[_opt|_smem]_cuda,
+ * modulated_deformable_col2im_coord[_opt]_cuda and the NHWC col2im family
+ * (csrc/binding.cpp:13-62, :80-140; used by ModulatedDeformConv2dFunction.
+ * backward, modulated_deform_conv.py:405-499, and col2im_nhwc,
+ * dcn_split_nhwc.py:48-120).  ACCUMULATES, as the reference's atomics do:
+ *   grad_input  [b, c, h, w]        += dcol * mask * (bilinear corner weight)
+ *   grad_offset [b, 2*(gi*T+t)+{0,1}, oh, ow] += mask * sum_c dcol * d(bilinear)/d(h, w)
+ *   grad_mask   [b, gi*T+t, oh, ow] += sum_c dcol * bilinear   (* sigmoid'(z)
+ *                                       when mask_is_logit)
+ * Any of grad_input / grad_offset / grad_mask may be NULL to skip it; input
+ * may be NULL when only grad_input is wanted (the corner values feed only the
+ * coordinate gradients).
+ * Samples outside the bilinear gate contribute nothing.  grad_input uses
+ * floating-point atomics (last bits vary between runs, as in the reference).
+ */
+BEVK_API int bevk_dcn_col2im(const bevk_dcn_col2im_args *args, const void *input,
+                             const void *offset, const void *mask, const void *dcol,
+                             void *grad_input, void *grad_offset, void *grad_mask,
+                             bevk_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Multi-scale deformable attention, forward                                */
 /* ------------------------------------------------------------------------ */
 
