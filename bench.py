@@ -315,6 +315,30 @@ def bench_dcn(cfg_name, steps, warmup, device, seed, img0, stream, dist=None, cl
                 sets=sets)
 
 
+def bench_dcn_bwd(cfg_name, steps, warmup, device, seed, stream):
+    """DCN backward as autograd runs it: dO . W^T (GEMM), the col2im scatter
+    into grad_input / grad_offset / grad_mask, the im2col gather and
+    dO^T . col (GEMM) for grad_weight, and grad_bias.  FLOPs counted: the two
+    GEMMs (2 x the forward's 2*M*N*K)."""
+    import torch
+    import modulated_deform_conv as mdc
+    cfg = DCN_CFGS[cfg_name]
+    flops, nbytes = dcn_work(cfg)
+    sets = dcn_sets(cfg, max(2, n_sets_for(3 * nbytes)), seed, 0, device)
+    for i, s in enumerate(sets):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 17 + i)
+        s["gout"] = torch.randn(s["out"].shape, generator=g, device=device).to(
+            s["out"].dtype).contiguous(memory_format=torch.channels_last)
+
+    def make(s):
+        return lambda: mdc.dcn_backward(s["x"], s["off"], s["mask"], s["w"], s["gout"],
+                                        1, 1, 1)
+
+    ms = graph_time([make(s) for s in sets], steps, warmup, stream)
+    return dict(ms=ms, flops=2 * flops, per_launch_s=ms / 1e3 / steps, n_sets=len(sets))
+
+
 def bench_dcn_e2e(cfg_name, steps, warmup, device, sets, stream, clocks=None, dist=None):
     """Public-API end-to-end: pinned host inputs -> device, modulated_deform_conv2d,
     output -> pinned host, every step."""
@@ -493,7 +517,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--only", choices=("cfg2", "cfg3", "cfg4", "cfg5", "bwd_cfg4", "bwd_cfg5"),
+    ap.add_argument("--only", choices=("cfg2", "cfg3", "cfg4", "cfg5", "bwd_cfg2", "bwd_cfg3",
+                                       "bwd_cfg4", "bwd_cfg5"),
                     help="time one workload's kernel only (profiling runs: no e2e, "
                          "secondary or CPU legs; prints a reduced line)")
     args = ap.parse_args()
@@ -526,6 +551,9 @@ def main():
         if args.only in DCN_CFGS:
             r = bench_dcn(args.only, args.steps, args.warmup, device, seed, 0, stream, dist)
             del r["sets"]
+            extra = {"tflops": r["flops"] / r["per_launch_s"] / 1e12}
+        elif args.only in ("bwd_cfg2", "bwd_cfg3"):
+            r = bench_dcn_bwd(args.only[4:], args.steps, args.warmup, device, seed, stream)
             extra = {"tflops": r["flops"] / r["per_launch_s"] / 1e12}
         elif args.only.startswith("bwd_"):
             r = bench_msda_bwd(args.only[4:], args.steps, args.warmup, device, seed, stream)
@@ -583,6 +611,15 @@ def main():
                 "algorithmic_GBps": gbs, "frac_hbm_peak": gbs / peaks["hbm_gbs"],
                 "roofline_us": r["bytes"] / (peaks["hbm_gbs"] * 1e9) * 1e6,
                 "traffic": _traffic(f"msda_fwd {name}")}
+            torch.cuda.empty_cache()
+        for name in ("cfg2", "cfg3"):
+            r = bench_dcn_bwd(name, min(k2, 100), args.warmup, device, seed + 4, stream)
+            a = r["flops"] / r["per_launch_s"] / 1e12
+            secondary[f"dcn_bwd_{name}"] = {
+                "workload": DCN_CFGS[name]["desc"].replace(" fwd", " bwd") +
+                            " (all five gradients)",
+                "us_per_call": r["per_launch_s"] * 1e6, "tflops": a,
+                "frac_tensor_peak": a / peaks["bf16_tflops"]}
             torch.cuda.empty_cache()
         for name in ("cfg4", "cfg5"):
             r = bench_msda_bwd(name, min(k2, 200), args.warmup, device, seed + 3, stream)

@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "bevk_modulated_deformable_im2col",
     "bevk_modulated_deformable_im2col_opt",
     "bevk_modulated_deformable_im2col_nhwc",
+    "bevk_dcn_columns",
     "bevk_dcn_col2im",
     "bevk_ms_deform_attn_forward",
     "bevk_ms_deform_attn_backward_workspace_bytes",
@@ -119,6 +120,8 @@ def lib():
     L.bevk_dcn_forward.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp, sz, vp]
     L.bevk_dcn_forward_noalloc.restype = i
     L.bevk_dcn_forward_noalloc.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp]
+    L.bevk_dcn_columns.restype = i
+    L.bevk_dcn_columns.argtypes = [pp, vp, vp, vp, vp, i, vp]
     L.bevk_dcn_col2im.restype = i
     L.bevk_dcn_col2im.argtypes = [ctypes.POINTER(DcnCol2imArgs), vp, vp, vp, vp, vp, vp, vp, vp]
     col_args = [vp, vp, vp] + [i] * 15

@@ -350,6 +350,25 @@ BEVK_API int bevk_ms_deform_attn_forward(const void *value, const int64_t *spati
                              reinterpret_cast<cudaStream_t>(stream));
 }
 
+BEVK_API int bevk_dcn_columns(const bevk_dcn_problem *p, const void *input,
+                              const void *offset, const void *mask, void *col, int layout,
+                              bevk_stream_t stream) {
+  clear_error();
+  if (!p || !input || !offset || !mask || !col)
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "dcn_columns: null pointer");
+  if (layout != 0 && layout != 1)
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "dcn_columns: layout must be 0 or 1");
+  bevk_dcn_problem pr = *p;
+  pr.out_channels = 1;
+  pr.groups = 1;
+  DcnDims d;
+  const int st = dcn_dims(&pr, &d);
+  if (st != BEVK_OK) return st;
+  if (d.M == 0) return BEVK_OK;
+  return launch_dcn_im2col(&pr, d, input, offset, mask, col, layout,
+                           reinterpret_cast<cudaStream_t>(stream));
+}
+
 BEVK_API int bevk_dcn_col2im(const bevk_dcn_col2im_args *args, const void *input,
                              const void *offset, const void *mask, const void *dcol,
                              void *grad_input, void *grad_offset, void *grad_mask,

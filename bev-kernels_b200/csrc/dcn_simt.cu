@@ -281,6 +281,43 @@ im2col_kernel(SimtParams p, const T *__restrict__ x, const T *__restrict__ off,
   }
 }
 
+// NHWC column matrix col[m, t*C + c] from channel-contiguous input (one
+// deformable group): one warp per (pixel, tap), lanes over the channels in
+// 16-byte vectors, so corner reads and column writes are whole-warp
+// contiguous segments.  Units run taps fastest, so consecutive warps write
+// consecutive parts of a pixel's column row.
+template <typename T>
+__global__ void __launch_bounds__(256)
+im2col_nhwc_vec_kernel(SimtParams p, const T *__restrict__ x, const T *__restrict__ off,
+                       const T *__restrict__ msk, T *__restrict__ col) {
+  constexpr int V = 16 / sizeof(T);
+  const int64_t unit = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (unit >= p.M * p.T) return;
+  const int lane = threadIdx.x & 31;
+  const int t = static_cast<int>(unit % p.T);
+  const int64_t m = unit / p.T;
+  const TapGeom<float> g = tap_geometry<float>(p, off, msk, m, t, 0);
+  T *dst = col + m * p.T * p.Cin + static_cast<int64_t>(t) * p.Cin;
+  for (int c = lane * V; c < p.Cin; c += 32 * V) {
+    float acc[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) acc[v] = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (g.w[q] == 0.f) continue;
+      const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(x + g.off[q] + c));
+      const T *e = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+      for (int v = 0; v < V; ++v) acc[v] = fmaf(g.w[q], ld_f<T>(e + v), acc[v]);
+    }
+    uint4 outv;
+    T *o = reinterpret_cast<T *>(&outv);
+#pragma unroll
+    for (int v = 0; v < V; ++v) o[v] = store_cast<T, float>(acc[v]);
+    *reinterpret_cast<uint4 *>(dst + c) = outv;
+  }
+}
+
 template <>
 __global__ void __launch_bounds__(256)
 im2col_kernel<double>(SimtParams p, const double *__restrict__ x, const double *__restrict__ off,
@@ -350,6 +387,20 @@ int launch_im2col_typed(const bevk_dcn_problem *pr, const DcnDims &d, const void
                         cudaStream_t stream) {
   const SimtParams p = make_params(pr, d);
   const int64_t MT = d.M * d.T;
+  if constexpr (sizeof(T) <= 4) {
+    constexpr int V = 16 / sizeof(T);
+    const bool vec = layout == 1 && d.dg == 1 && d.Cin % V == 0 && pr->input_strides[1] == 1 &&
+                     pr->input_strides[0] % V == 0 && pr->input_strides[2] % V == 0 &&
+                     pr->input_strides[3] % V == 0 && aligned(x, 16) && aligned(col, 16);
+    if (vec) {
+      const int64_t blocks = (MT * 32 + 255) / 256;
+      if (blocks > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "im2col: grid too large");
+      im2col_nhwc_vec_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+          p, static_cast<const T *>(x), static_cast<const T *>(off), static_cast<const T *>(msk),
+          static_cast<T *>(col));
+      return check_launch("im2col_nhwc_vec_kernel");
+    }
+  }
   const int cblock = 64;
   const int64_t bx = (MT + 255) / 256;
   const int by = (d.Cin + cblock - 1) / cblock;

@@ -377,6 +377,35 @@ void dcn_col2im(const Tensor &dcol, const c10::optional<Tensor> &input, const Te
                 gm.defined() ? &gm : nullptr, false, "dcn_col2im");
 }
 
+// Deformable columns of NCHW-shaped tensors in any memory format: layout 0
+// [C*kH*kW, M], layout 1 [M, kH*kW*C].
+Tensor dcn_columns(const Tensor &input, const Tensor &offset, const Tensor &mask,
+                   int64_t kernel_h, int64_t kernel_w, int64_t stride_h, int64_t stride_w,
+                   int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w,
+                   int64_t deform_groups, int64_t layout) {
+  check_cuda(input, "input");
+  check_same_device(input, offset, "offset");
+  check_same_device(input, mask, "mask");
+  TORCH_CHECK(offset.scalar_type() == input.scalar_type() &&
+                  mask.scalar_type() == input.scalar_type(),
+              "bevk: dcn_columns: input / offset / mask must share a dtype");
+  const int64_t T = kernel_h * kernel_w;
+  const int64_t M = offset.size(0) * offset.size(2) * offset.size(3);
+  Tensor col = layout == 0 ? at::empty({input.size(1) * T, M}, input.options())
+                           : at::empty({M, T * input.size(1)}, input.options());
+  bevk_dcn_problem p = make_problem(input, offset, mask, Tensor(), 1, static_cast<int>(kernel_h),
+                                    static_cast<int>(kernel_w), static_cast<int>(stride_h),
+                                    static_cast<int>(stride_w), static_cast<int>(pad_h),
+                                    static_cast<int>(pad_w), static_cast<int>(dil_h),
+                                    static_cast<int>(dil_w), 1, static_cast<int>(deform_groups),
+                                    false, false);
+  const c10::cuda::CUDAGuard guard(input.device());
+  check_status(bevk_dcn_columns(&p, input.data_ptr(), offset.data_ptr(), mask.data_ptr(),
+                                col.data_ptr(), static_cast<int>(layout), current_stream(input)),
+               "dcn_columns");
+  return col;
+}
+
 int64_t watchdog(int64_t device) {
   unsigned int code = 0;
   bevk_device_watchdog(static_cast<int>(device), &code);
@@ -428,6 +457,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("kernel_w"), py::arg("stride_h"), py::arg("stride_w"), py::arg("pad_h"),
         py::arg("pad_w"), py::arg("dil_h"), py::arg("dil_w"), py::arg("deform_groups"),
         py::arg("grad_input"), py::arg("grad_offset"), py::arg("grad_mask"));
+  m.def("dcn_columns", &dcn_columns,
+        "Deformable column matrix (layout 0: [C*kH*kW, M], 1: [M, kH*kW*C])",
+        py::arg("input"), py::arg("offset"), py::arg("mask"), py::arg("kernel_h"),
+        py::arg("kernel_w"), py::arg("stride_h"), py::arg("stride_w"), py::arg("pad_h"),
+        py::arg("pad_w"), py::arg("dil_h"), py::arg("dil_w"), py::arg("deform_groups"),
+        py::arg("layout"));
   m.def("watchdog", &watchdog, "Read and clear the device watchdog word (0 = clean)",
         py::arg("device"));
   m.def("version", []() { return bevk_version(); });

@@ -4,7 +4,13 @@ from .modulated_deform_conv import (  # noqa: F401
     ModulatedDeformConv2d,
     ModulatedDeformConv2dFunction,
     ModulatedDeformConv2dPack,
+    dcn_backward,
     dcn_forward_into,
+    ext_modulated_deformable_col2im,
+    ext_modulated_deformable_col2im_coord,
+    ext_modulated_deformable_col2im_coord_opt,
+    ext_modulated_deformable_col2im_opt,
+    ext_modulated_deformable_col2im_smem,
     ext_modulated_deformable_im2col,
     ext_modulated_deformable_im2col_opt,
     modulated_deform_conv2d,
@@ -25,6 +31,12 @@ __all__ = [
     "modulated_deform_conv2d",
     "ext_modulated_deformable_im2col",
     "ext_modulated_deformable_im2col_opt",
+    "ext_modulated_deformable_col2im",
+    "ext_modulated_deformable_col2im_opt",
+    "ext_modulated_deformable_col2im_smem",
+    "ext_modulated_deformable_col2im_coord",
+    "ext_modulated_deformable_col2im_coord_opt",
+    "dcn_backward",
     "DCNSplitNHWCFunction",
     "dcn_apply_nchw",
     "dcn_split_nhwc",

@@ -77,6 +77,60 @@ def ext_modulated_deformable_im2col_opt(data_im, data_offset, data_mask, kernel_
     return data_col
 
 
+def _col2im(entry, data_col, data_offset, data_mask, batch_size, channels, height, width,
+            kernel_h, kernel_w, pad_h, pad_w, stride_h, stride_w, dilation_h, dilation_w,
+            deformable_group):
+    ext = _load_ext()
+    height_col = _out_size(height, pad_h, dilation_h, kernel_h, stride_h)
+    width_col = _out_size(width, pad_w, dilation_w, kernel_w, stride_w)
+    grad_im = data_col.new_zeros(batch_size, channels, height, width)
+    getattr(ext, entry)(data_col.contiguous(), data_offset, data_mask, batch_size, channels,
+                        height, width, height_col, width_col, kernel_h, kernel_w, pad_h, pad_w,
+                        stride_h, stride_w, dilation_h, dilation_w, deformable_group, grad_im)
+    return grad_im
+
+
+def ext_modulated_deformable_col2im(*args):
+    """Column gradient [C*kH*kW, B*Ho*Wo] -> grad_im [B, C, H, W]
+    (modulated_deform_conv.py:115-134; same arguments)."""
+    return _col2im("modulated_deformable_col2im_cuda", *args)
+
+
+def ext_modulated_deformable_col2im_opt(*args):
+    """As ext_modulated_deformable_col2im (modulated_deform_conv.py:73-92)."""
+    return _col2im("modulated_deformable_col2im_opt_cuda", *args)
+
+
+def ext_modulated_deformable_col2im_smem(*args):
+    """As ext_modulated_deformable_col2im (modulated_deform_conv.py:94-113)."""
+    return _col2im("modulated_deformable_col2im_smem_cuda", *args)
+
+
+def _col2im_coord(entry, data_col, data_im, data_offset, data_mask, kernel_h, kernel_w, pad_h,
+                  pad_w, stride_h, stride_w, dilation_h, dilation_w, deformable_group):
+    ext = _load_ext()
+    batch_size, channels, height, width = data_im.shape
+    height_col = _out_size(height, pad_h, dilation_h, kernel_h, stride_h)
+    width_col = _out_size(width, pad_w, dilation_w, kernel_w, stride_w)
+    grad_offset = data_offset.new_zeros(data_offset.shape)
+    grad_mask = data_mask.new_zeros(data_mask.shape)
+    getattr(ext, entry)(data_col.contiguous(), data_im, data_offset, data_mask, batch_size,
+                        channels, height, width, height_col, width_col, kernel_h, kernel_w,
+                        pad_h, pad_w, stride_h, stride_w, dilation_h, dilation_w,
+                        deformable_group, grad_offset, grad_mask)
+    return grad_offset, grad_mask
+
+
+def ext_modulated_deformable_col2im_coord(*args):
+    """Column gradient -> (grad_offset, grad_mask) (modulated_deform_conv.py:136-156)."""
+    return _col2im_coord("modulated_deformable_col2im_coord_cuda", *args)
+
+
+def ext_modulated_deformable_col2im_coord_opt(*args):
+    """As ext_modulated_deformable_col2im_coord (modulated_deform_conv.py:158-182)."""
+    return _col2im_coord("modulated_deformable_col2im_coord_opt_cuda", *args)
+
+
 # ---------------------------------------------------------------------------
 # Packed weights
 # ---------------------------------------------------------------------------
@@ -225,17 +279,19 @@ def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dila
             grad_offset = goff.to(offset.dtype)
             grad_mask = gmsk.to(mask.dtype)
     if need_weight:
-        # reference column matrix [C*T, M] (k = c*T + t) from the im2col kernel
-        col = input.new_empty(C * T, M)
-        ext.modulated_deformable_im2col_opt_cuda(
-            input.contiguous(), offset.contiguous(), mask.contiguous(), B, C, H, W, Ho, Wo,
-            kH, kW, ph, pw, sh, sw, dh, dw, deform_groups, col)
+        # NHWC column matrix [M, T*C] (k = t*C + c; aligned leading dimensions
+        # for the GEMM) gathered straight from the input in its own layout
+        col = ext.dcn_columns(input, offset, mask, kH, kW, sh, sw, ph, pw, dh, dw,
+                              deform_groups, 1)
         if G == 1:
-            gw = torch.mm(go.t(), col.t())
+            gw = torch.mm(go.t(), col)                                   # [Cout, T*C]
+            gw = gw.view(Cout, kH, kW, C).permute(0, 3, 1, 2)
         else:
+            colg = col.view(M, T, G, Cg)
             gw = torch.cat([torch.mm(go[:, g * Coutg:(g + 1) * Coutg].t(),
-                                     col[g * Cg * T:(g + 1) * Cg * T].t()) for g in range(G)], 0)
-        grad_weight = gw.view_as(weight).to(weight.dtype)
+                                     colg[:, :, g].reshape(M, T * Cg)) for g in range(G)], 0)
+            gw = gw.view(Cout, kH, kW, Cg).permute(0, 3, 1, 2)
+        grad_weight = gw.contiguous().to(weight.dtype)
     if need_bias:
         grad_bias = go.to(acc).sum(0).to(dt)
     return grad_input, grad_offset, grad_mask, grad_weight, grad_bias

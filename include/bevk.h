@@ -208,6 +208,18 @@ BEVK_API int bevk_modulated_deformable_im2col_nhwc(
     int deformable_group, int offset_last_dim, void *data_col, int dtype,
     bevk_stream_t stream);
 
+/*
+ * Deformable column matrix of a problem with any input / offset / mask
+ * strides (problem fields as for bevk_dcn_forward; out_channels, groups,
+ * output_strides and has_bias unused): layout 0 writes the reference's
+ * [C*kH*kW, M] matrix (modulated_deform_conv.py:370), layout 1 the NHWC
+ * matrix [M, kH*kW*C] with k = t*C + c (dcn_split_nhwc.py:21-45).  Every
+ * element is written.  Used for the weight gradient of the backward.
+ */
+BEVK_API int bevk_dcn_columns(const bevk_dcn_problem *p, const void *input,
+                              const void *offset, const void *mask, void *col,
+                              int layout, bevk_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* DCNv2 backward: column scatter                                           */
 /* ------------------------------------------------------------------------ */

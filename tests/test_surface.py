@@ -10,20 +10,35 @@ import ms_deform_attn
 def test_reference_exports_present():
     for name in ("ModulatedDeformConv2dFunction", "ModulatedDeformConv2d",
                  "ModulatedDeformConv2dPack", "modulated_deform_conv2d", "dcn_apply_nchw",
-                 "dcn_split_nhwc", "gather_cols_nhwc", "DCNSplitNHWCFunction"):
+                 "dcn_split_nhwc", "gather_cols_nhwc", "DCNSplitNHWCFunction",
+                 # modulated_deform_conv/__init__.py:2-10 of the reference
+                 "ext_modulated_deformable_col2im_opt", "ext_modulated_deformable_col2im_smem",
+                 "ext_modulated_deformable_col2im_coord_opt"):
         assert hasattr(mdc, name), name
     import msda_musa_opt2
     assert msda_musa_opt2.ms_deform_attn_forward is ms_deform_attn.ms_deform_attn_forward
+    assert msda_musa_opt2.ms_deform_attn_backward is ms_deform_attn.ms_deform_attn_backward
     assert hasattr(ms_deform_attn, "MultiScaleDeformableAttnFunction")
 
 
 def test_extension_exports_reference_op_names():
     import _modulated_deform_conv_ext as ext
     for name in ("modulated_deformable_im2col_cuda", "modulated_deformable_im2col_opt_cuda",
-                 "modulated_deformable_im2col_nhwc_cuda", "dcn_forward", "dcn_pack_weight"):
+                 "modulated_deformable_im2col_nhwc_cuda", "dcn_forward", "dcn_pack_weight",
+                 # backward ops, csrc/binding.cpp:146-191
+                 "modulated_deformable_col2im_cuda", "modulated_deformable_col2im_opt_cuda",
+                 "modulated_deformable_col2im_smem_cuda", "modulated_deformable_col2im_coord_cuda",
+                 "modulated_deformable_col2im_coord_opt_cuda",
+                 "modulated_deformable_col2im_nhwc_cuda",
+                 "modulated_deformable_col2im_coord_nhwc_cuda",
+                 "modulated_deformable_gradx_smem_nhwc_cuda",
+                 "modulated_deformable_gradx_gather_nhwc_cuda",
+                 "modulated_deformable_col2im_fused_smem_nhwc_cuda",
+                 "modulated_deformable_col2im_perelem_nhwc_cuda",
+                 "modulated_deformable_col2im_perelem_smem_nhwc_cuda"):
         assert hasattr(ext, name), name
     import _ms_deform_attn_ext as mext
-    assert hasattr(mext, "forward")
+    assert hasattr(mext, "forward") and hasattr(mext, "backward")
 
 
 def test_module_parameters_match_mmcv_layout():
