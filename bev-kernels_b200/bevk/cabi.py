@@ -67,6 +67,7 @@ class DcnProblem(ctypes.Structure):
         ("output_strides", ctypes.c_int64 * 4),
         ("mask_is_logit", ctypes.c_int),
         ("has_bias", ctypes.c_int),
+        ("act_relu", ctypes.c_int),
     ]
 
 

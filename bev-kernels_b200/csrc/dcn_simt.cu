@@ -60,7 +60,7 @@ struct SimtParams {
   int Ho, Wo, Cin_g, Cout_g, Cin_g_pad, cpdg, groups;
   int64_t M;
   int64_t xs[4], os[4], ms[4], ys[4];
-  int mask_is_logit, has_bias;
+  int mask_is_logit, has_bias, act_relu;
 };
 
 // Tap geometry of one (pixel, tap, deformable group): element offsets of the
@@ -205,6 +205,7 @@ dcn_fwd_simt_kernel(SimtParams p, const T *__restrict__ x, const T *__restrict__
       const int cog = grp * p.Cout_g + co;
       Acc v = acc[i][jj];
       if (p.has_bias) v += ld_acc<Acc>(bias + cog);
+      if (p.act_relu && v < Acc(0)) v = Acc(0);
       yb[static_cast<int64_t>(cog) * p.ys[1]] = store_cast<T, Acc>(v);
     }
   }
@@ -361,6 +362,7 @@ SimtParams make_params(const bevk_dcn_problem *pr, const DcnDims &d) {
   }
   p.mask_is_logit = pr->mask_is_logit;
   p.has_bias = pr->has_bias;
+  p.act_relu = pr->act_relu;
   return p;
 }
 

@@ -72,7 +72,7 @@ struct TcParams {
   int Cin, H, W, Ho, Wo, Cout, kW, T;
   int sh, sw, ph, pw, dh, dw;
   int M, Cin_pad, n_cc, n_k, n_tiles_n;
-  int mask_is_logit, has_bias;
+  int mask_is_logit, has_bias, act_relu;
   int xs0, xs2, xs3;        // input strides (channel stride is 1)
   int64_t os[4], ms[4], ys[4];
 };
@@ -483,6 +483,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
           for (int jj = 0; jj < kChunk; ++jj) {
             v[jj] = __uint_as_float(r[jj]);
             if (p.has_bias && co0 + jj < p.Cout) v[jj] += ld_float(bias + co0 + jj);
+            if (p.act_relu) v[jj] = fmaxf(v[jj], 0.f);
           }
           if (vec_out && co0 + kChunk <= p.Cout) {
 #pragma unroll
@@ -711,6 +712,7 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
                 (mode == kModeNSplit ? 2 * BN : BN);
   p.mask_is_logit = pr->mask_is_logit;
   p.has_bias = pr->has_bias;
+  p.act_relu = pr->act_relu;
   p.xs0 = static_cast<int>(xs[0]); p.xs2 = static_cast<int>(xs[2]); p.xs3 = static_cast<int>(xs[3]);
   for (int i = 0; i < 4; ++i) {
     p.os[i] = pr->offset_strides[i];

@@ -147,7 +147,7 @@ void dcn_forward(const Tensor &input, const Tensor &offset, const Tensor &mask,
                  const Tensor &packed_weight, const c10::optional<Tensor> &bias, Tensor output,
                  int64_t kernel_h, int64_t kernel_w, int64_t stride_h, int64_t stride_w,
                  int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w, int64_t groups,
-                 int64_t deform_groups, bool mask_is_logit) {
+                 int64_t deform_groups, bool mask_is_logit, bool act_relu) {
   check_cuda(input, "input");
   for (const Tensor *t : std::initializer_list<const Tensor *>{&offset, &mask, &packed_weight, &output})
     check_same_device(input, *t, "dcn tensor");
@@ -172,6 +172,7 @@ void dcn_forward(const Tensor &input, const Tensor &offset, const Tensor &mask,
                                     static_cast<int>(dil_h), static_cast<int>(dil_w),
                                     static_cast<int>(groups), static_cast<int>(deform_groups),
                                     mask_is_logit, has_bias);
+  p.act_relu = act_relu ? 1 : 0;
   int ho = 0, wo = 0;
   check_status(bevk_dcn_output_size(&p, &ho, &wo), "dcn_forward");
   TORCH_CHECK(output.size(0) == p.batch && output.size(2) == ho && output.size(3) == wo,
@@ -428,7 +429,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bias"), py::arg("output"), py::arg("kernel_h"), py::arg("kernel_w"),
         py::arg("stride_h"), py::arg("stride_w"), py::arg("pad_h"), py::arg("pad_w"),
         py::arg("dil_h"), py::arg("dil_w"), py::arg("groups"), py::arg("deform_groups"),
-        py::arg("mask_is_logit") = false);
+        py::arg("mask_is_logit") = false, py::arg("act_relu") = false);
   // backward column scatter under the reference's op names (csrc/binding.cpp:146-191)
   for (const char *name : {"modulated_deformable_col2im_cuda", "modulated_deformable_col2im_opt_cuda",
                            "modulated_deformable_col2im_smem_cuda"})

@@ -62,11 +62,12 @@ def _forward_nhwc(x_nhwc, w_off, b_off, weight, bias, stride, padding, dilation,
         weight, bias = _fold_bn(weight, bias, bn_scale, bn_shift)
     weight = weight.to(x_nhwc.dtype)
     out = torch.empty(B, Ho, Wo, Cout, device=x_nhwc.device, dtype=x_nhwc.dtype)
+    # the FrozenBN affine is folded into weight / bias; its ReLU runs in the
+    # kernel's epilogue
     dcn_forward_into(x_view, y[:, :2 * T], y[:, 2 * T:], weight,
                      None if bias is None else bias.to(x_nhwc.dtype), out.permute(0, 3, 1, 2),
-                     stride, padding, dilation, mask_is_logit=True)
-    if bn_scale is not None and act_relu:
-        out.relu_()
+                     stride, padding, dilation, mask_is_logit=True,
+                     act_relu=bn_scale is not None and bool(act_relu))
     return out, y
 
 

@@ -156,11 +156,12 @@ def packed_weight(weight: torch.Tensor, groups: int = 1) -> torch.Tensor:
 
 
 def dcn_forward_into(input, offset, mask, weight, bias, output, stride, padding, dilation,
-                     groups=1, deform_groups=1, mask_is_logit=False):
+                     groups=1, deform_groups=1, mask_is_logit=False, act_relu=False):
     """Fused DCNv2 forward writing into ``output`` ([B, Cout, Ho, Wo], any strides).
 
     ``input``/``offset``/``mask`` may be NCHW-contiguous or channels-last views;
-    ``mask_is_logit`` applies the sigmoid on load (raw offset-conv output).
+    ``mask_is_logit`` applies the sigmoid on load (raw offset-conv output);
+    ``act_relu`` applies max(0, .) in the kernel's epilogue.
     """
     kh, kw = weight.shape[2], weight.shape[3]
     sh, sw = _pair(stride)
@@ -168,7 +169,7 @@ def dcn_forward_into(input, offset, mask, weight, bias, output, stride, padding,
     dh, dw = _pair(dilation)
     _load_ext().dcn_forward(input, offset, mask, packed_weight(weight, groups), bias, output,
                             kh, kw, sh, sw, ph, pw, dh, dw, int(groups), int(deform_groups),
-                            bool(mask_is_logit))
+                            bool(mask_is_logit), bool(act_relu))
     return output
 
 

@@ -98,6 +98,9 @@ typedef struct bevk_dcn_problem {
                                 applied on load (the fused offset-conv output
                                 path of dcn_split_nhwc.py:159-174)             */
   int has_bias;
+  int act_relu;              /* 1: output = max(0, conv + bias), the ReLU of a
+                                FrozenBN+ReLU epilogue whose affine is folded
+                                into weight and bias (dcn_split_nhwc.py:185-199) */
 } bevk_dcn_problem;
 
 /* Output height/width of a problem (BEVK_ERR_INVALID_ARGUMENT if <= 0). */

@@ -198,3 +198,75 @@ def test_split_nhwc_backward(cuda):
                             (tens[3].grad, torch.from_numpy(gw), "weight"),
                             (tens[4].grad, torch.from_numpy(gb), "bias")):
         assert rel_l2(got, want) <= 2e-5, (name, rel_l2(got, want))
+
+
+def _split_reference(x, w_off, b_off, w, b, bn_scale, bn_shift):
+    """CPU composite: offset conv (torch, fp32), oracle DCN forward, BN affine, ReLU."""
+    import torch.nn.functional as F
+    T = 9
+    y = F.conv2d(x.permute(0, 3, 1, 2).float(), w_off.float(), b_off.float(), 1, 1, 1)
+    off, mask = y[:, :2 * T], torch.sigmoid(y[:, 2 * T:])
+    z = torch.from_numpy(oracle.dcn_forward(x.permute(0, 3, 1, 2).float().numpy(),
+                                            off.numpy(), mask.numpy(), w.float().numpy(),
+                                            b.float().numpy(), 1, 1, 1))
+    z = z * bn_scale.float().view(1, -1, 1, 1) + bn_shift.float().view(1, -1, 1, 1)
+    return torch.relu(z).permute(0, 2, 3, 1), y, off, mask
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16], ids=["f32_simt", "f16_tc"])
+def test_split_nhwc_bn_relu_epilogue(cuda, dt):
+    """FrozenBN folded into weight / bias and the ReLU applied in the kernel's
+    epilogue (dcn_split_nhwc.py:185-199)."""
+    from modulated_deform_conv import dcn_split_nhwc
+    g = torch.Generator().manual_seed(71)
+    B, C, H, W, Cout, T = 2, 64, 9, 10, 64, 9
+    x = torch.randn(B, H, W, C, generator=g)
+    w_off = torch.randn(3 * T, C, 3, 3, generator=g) * 0.03
+    b_off = torch.randn(3 * T, generator=g) * 0.5
+    w = torch.randn(Cout, C, 3, 3, generator=g) * 0.05
+    b = torch.randn(Cout, generator=g)
+    scale = torch.rand(Cout, generator=g) + 0.5
+    shift = torch.randn(Cout, generator=g)
+    xs, wos, bos, ws, bs = (t.to(dt) for t in (x, w_off, b_off, w, b))
+    want = _split_reference(xs, wos, bos, ws, bs, scale, shift)[0]
+    prev = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        out = dcn_split_nhwc(*(t.to(cuda) for t in (xs, wos, bos, ws, bs)), 1, 1, 1,
+                             scale.to(cuda), shift.to(cuda), True)
+    finally:
+        torch.backends.cudnn.allow_tf32 = prev
+    assert (out >= 0).all()
+    tol = FP32_REL * 3 if dt == torch.float32 else HALF_REL
+    assert rel_l2(out.float(), want) <= tol, rel_l2(out.float(), want)
+
+
+def test_split_nhwc_bn_relu_backward(cuda):
+    """Backward through the folded BN + ReLU epilogue: dO is masked by the ReLU
+    and scaled by the BN scale (dcn_split_nhwc.py:256-266), fp32."""
+    from modulated_deform_conv import dcn_split_nhwc
+    g = torch.Generator().manual_seed(72)
+    B, C, H, W, Cout, T = 1, 16, 8, 9, 12, 9
+    x = torch.randn(B, H, W, C, generator=g)
+    w_off = torch.randn(3 * T, C, 3, 3, generator=g) * 0.05
+    b_off = torch.randn(3 * T, generator=g) * 0.5
+    w = torch.randn(Cout, C, 3, 3, generator=g) * 0.1
+    b = torch.randn(Cout, generator=g)
+    scale = torch.rand(Cout, generator=g) + 0.5
+    shift = torch.randn(Cout, generator=g) * 0.2
+    gout = torch.randn(B, H, W, Cout, generator=g)
+    out_ref, y, off, mask = _split_reference(x, w_off, b_off, w, b, scale, shift)
+    dz = (gout * (out_ref > 0)).permute(0, 3, 1, 2) * scale.view(1, -1, 1, 1)   # d/d(conv+bias)
+    gx, goff, gmask, gw, gb = oracle.dcn_backward(
+        x.permute(0, 3, 1, 2).numpy(), off.numpy(), mask.numpy(), w.numpy(), dz.numpy(), 1, 1, 1)
+    prev = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        tens = [t.to(cuda).requires_grad_() for t in (x, w, b)]
+        out = dcn_split_nhwc(tens[0], w_off.to(cuda), b_off.to(cuda), tens[1], tens[2], 1, 1, 1,
+                             scale.to(cuda), shift.to(cuda), True)
+        out.backward(gout.to(cuda))
+    finally:
+        torch.backends.cudnn.allow_tf32 = prev
+    assert rel_l2(tens[1].grad, torch.from_numpy(gw)) <= 2e-5
+    assert rel_l2(tens[2].grad, torch.from_numpy(gb)) <= 2e-5
