@@ -340,8 +340,13 @@ def bench_dcn_bwd(cfg_name, steps, warmup, device, seed, stream):
 
 
 def bench_dcn_e2e(cfg_name, steps, warmup, device, sets, stream, clocks=None, dist=None):
-    """Public-API end-to-end: pinned host inputs -> device, modulated_deform_conv2d,
-    output -> pinned host, every step."""
+    """Public-API end-to-end: every step copies its inputs from pinned host memory
+    to the device, runs modulated_deform_conv2d and reads its output back into
+    pinned host memory.  The steps are pipelined the way an inference loop runs
+    them: the host->device copy of step k+1 and the device->host copy of step
+    k-1 run on their own streams while step k computes (two buffer sets,
+    ordered by events), so the per-step time is that of the slowest of the
+    three, not their sum."""
     import torch
     import modulated_deform_conv as mdc
     cfg = DCN_CFGS[cfg_name]
@@ -350,24 +355,39 @@ def bench_dcn_e2e(cfg_name, steps, warmup, device, sets, stream, clocks=None, di
     ho = s0["off"].cpu().pin_memory()
     hm = s0["mask"].cpu().pin_memory()
     w = s0["w"]
-    dx = torch.empty_like(s0["x"])
-    do = torch.empty_like(s0["off"])
-    dm = torch.empty_like(s0["mask"])
     B, Co, H, W = cfg["B"], cfg["Cout"], cfg["H"], cfg["W"]
-    hout = torch.empty(B, Co, H, W, dtype=s0["x"].dtype).pin_memory()
+    dev_in = [(torch.empty_like(s0["x"]), torch.empty_like(s0["off"]),
+               torch.empty_like(s0["mask"])) for _ in range(2)]
+    hout = [torch.empty(B, Co, H, W, dtype=s0["x"].dtype).pin_memory() for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in (hx, ho, hm))
-    d2h = hout.numel() * hout.element_size()
+    d2h = hout[0].numel() * hout[0].element_size()
+    s_in, s_comp, s_out = torch.cuda.Stream(), stream, torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    ys = [None, None]   # step k's output stays referenced until step k+2 (read back by then)
 
-    def step():
-        dx.copy_(hx, non_blocking=True)
-        do.copy_(ho, non_blocking=True)
-        dm.copy_(hm, non_blocking=True)
-        y = mdc.modulated_deform_conv2d(dx, do, dm, w, None, 1, 1, 1)
-        hout.copy_(y, non_blocking=True)
+    def step(k):
+        i = k % 2
+        dx, do, dm = dev_in[i]
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_comp[i])               # step k-2 has consumed buffer set i
+            dx.copy_(hx, non_blocking=True)
+            do.copy_(ho, non_blocking=True)
+            dm.copy_(hm, non_blocking=True)
+            ev_in[i].record(s_in)
+        with torch.cuda.stream(s_comp):
+            s_comp.wait_event(ev_in[i])
+            s_comp.wait_event(ev_out[i])              # step k-2's output has been read back
+            ys[i] = mdc.modulated_deform_conv2d(dx, do, dm, w, None, 1, 1, 1)
+            ev_comp[i].record(s_comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_comp[i])
+            hout[i].copy_(ys[i], non_blocking=True)
+            ev_out[i].record(s_out)
 
-    with torch.cuda.stream(stream):
-        for _ in range(warmup):
-            step()
+    for k in range(warmup):
+        step(k)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist is not None:
@@ -375,11 +395,10 @@ def bench_dcn_e2e(cfg_name, steps, warmup, device, sets, stream, clocks=None, di
     torch.cuda.synchronize()
     ctx = clocks if clocks is not None else _Null()
     with ctx:
-        with torch.cuda.stream(stream):
-            start.record(stream)
-            for _ in range(steps):
-                step()
-            end.record(stream)
+        start.record(s_in)
+        for k in range(steps):
+            step(k)
+        end.record(s_out)                             # after the last read-back
         torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
@@ -655,7 +674,7 @@ def main():
             "roofline": roof,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "api": "modulated_deform_conv.modulated_deform_conv2d (pinned host in/out)",
+                    "api": "modulated_deform_conv.modulated_deform_conv2d (pinned host in/out every step; H2D of step k+1 and D2H of step k-1 overlap step k on separate streams)",
                     "clocks": e2e_clocks.summary()},
             "gpu_launches": args.steps,
             "clocks": clocks.summary(),
