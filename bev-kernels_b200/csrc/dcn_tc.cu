@@ -5,7 +5,7 @@
 //
 // One CTA computes a 128-pixel x BN-output-channel tile.  The reduction runs
 // over (tap, 64-channel chunk) stages:
-//   * 8 gather warps build the A stage in shared memory directly in the
+//   * 16 gather warps build the A stage in shared memory directly in the
 //     canonical K-major 128-byte-swizzled UMMA layout: 8 lanes cover one
 //     pixel's 64 channels (16-byte vector loads from NHWC input, one load per
 //     bilinear corner), interpolate (packed half2 FMA for fp16, fp32 FMA for
@@ -16,7 +16,7 @@
 //   * 1 MMA warp allocates the TMEM accumulator and issues, from one thread,
 //     tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) x 4 per stage,
 //     committing each stage back to its "empty" barrier;
-//   * the 8 gather warps then drain TMEM (tcgen05.ld 32x32b), add bias and
+//   * warps 0-15 then drain TMEM (tcgen05.ld 32x32b), add bias and
 //     store fp16/bf16 to any output layout.
 // Pipelining uses full/empty mbarrier rings.  Every wait is bounded (2 s);
 // a wait that gives up records its site in g_bevk_watchdog, raises a CTA-wide
@@ -55,9 +55,7 @@ namespace {
 constexpr int kBM = 128;           // pixels per tile (UMMA M)
 constexpr int kBK = 64;            // channels per stage (128 B of fp16/bf16)
 constexpr int kGatherWarps = 16;
-constexpr int kThreads = (kGatherWarps + 2) * 32;
-constexpr int kTmaWarp = kGatherWarps;
-constexpr int kMmaWarp = kGatherWarps + 1;
+constexpr int kEpilogueWarps = 16;  // warps 0-15: four per TMEM lane quadrant (w % 4)
 constexpr int kMaxTaps = 9;
 
 // Watchdog sites (low byte) -- identify which wait expired.
@@ -84,6 +82,54 @@ enum : int {
   kModeNSplit = 2,  // 2-CTA cluster per 128-pixel x 2*BN tile, A rows shared
 };
 
+// Warp roles.  A warp issues on SM sub-partition (warp index mod 4).
+// Isolated layout (21 warps): the TMA warp (7) and the MMA warp (3) have
+// sub-partition 3 to themselves (with idle warps 11, 15, 19) and the 16
+// gather warps fill sub-partitions 0-2.  A gather warp that shares a
+// sub-partition with the thread issuing tcgen05.mma (which blocks while the
+// tensor pipe is busy) or the TMA copies falls most of a stage behind the
+// others, and the slowest gather warp sets the pace of the pipeline.  The
+// price is the register budget: six warps on a sub-partition leave 80
+// registers a thread.  Compact layout (18 warps, 96 registers): gather warps
+// 0-15, TMA warp 16, MMA warp 17.
+template <bool ISO>
+struct Roles;
+template <>
+struct Roles<true> {
+  static constexpr int kWarps = 21, kMma = 3, kTma = 7;
+  __device__ static bool gather(int w) { return (w & 3) != 3; }
+  __device__ static int gather_index(int w) { return w - ((w + 1) >> 2); }
+};
+template <>
+struct Roles<false> {
+  static constexpr int kWarps = kGatherWarps + 2, kMma = kGatherWarps + 1, kTma = kGatherWarps;
+  __device__ static bool gather(int w) { return w < kGatherWarps; }
+  __device__ static int gather_index(int w) { return w; }
+};
+// Measured on B200 (cfg2 N-split 53.1 -> 56.2 us, cfg3 pair 82.9 -> 130 us):
+// the gather warps are issue-bound, so giving up a sub-partition costs more
+// than the lag it removes, and every schedule uses the compact layout.  The
+// isolated one is kept for experiments (BEVK_DCN_ISO_ROLES).
+__host__ __device__ constexpr bool iso_roles(int mode) {
+#ifdef BEVK_DCN_ISO_ROLES
+  return mode >= 0;
+#else
+  return mode < 0;
+#endif
+}
+template <int MODE>
+__host__ __device__ constexpr int tc_threads() {
+  return Roles<iso_roles(MODE)>::kWarps * 32;
+}
+// Gather warps that build one A stage: one row a thread, at most all of them
+// (VB = bytes a lane loads per corner; N-split CTAs gather 64 rows a stage).
+template <int MODE, int VB>
+__host__ __device__ constexpr int warps_per_stage() {
+  return ((MODE == kModeNSplit ? kBM / 2 : kBM) * 4 / VB) < kGatherWarps
+             ? (MODE == kModeNSplit ? kBM / 2 : kBM) * 4 / VB
+             : kGatherWarps;
+}
+
 template <int BN, int STAGES, bool PAIR>
 struct Smem {
   // In a CTA pair each CTA holds half of the B tile (BN/2 output channels).
@@ -94,8 +140,8 @@ struct Smem {
   static constexpr int kB = kA + STAGES * kABytes;
   static constexpr int kGW = kB + STAGES * kBBytes;          // 4 fp16 weights [T][BM]
   static constexpr int kGB = kGW + kMaxTaps * kBM * 8;       // packed base + mask [T][BM]
-  static constexpr int kBar = kGB + kMaxTaps * kBM * 4;      // full[S], wfull[S], empty[S], tmem_full
-  static constexpr int kMisc = kBar + (3 * STAGES + 1) * 8;  // tmem slot, abort flag
+  static constexpr int kBar = kGB + kMaxTaps * kBM * 4;      // full[S], empty[S], tmem_full
+  static constexpr int kMisc = kBar + (2 * STAGES + 1) * 8;  // tmem slot, abort flag
   static constexpr int kTotal = kMisc + 16;
   static constexpr int kAlloc = kTotal + 1024;               // 1024-byte alignment slack
 };
@@ -254,17 +300,22 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   const uint32_t sA = sbase + L::kA, sB = sbase + L::kB;
   uint2 *s_gw = reinterpret_cast<uint2 *>(smem + L::kGW);
   int *s_gb = reinterpret_cast<int *>(smem + L::kGB);
-  // full: A rows written by the gather warps (NSPLIT: this CTA's half).
-  // wfull: B stage landed (TMA bytes; NSPLIT: plus the other CTA's A half).
+  // full: one barrier per stage for everything the MMA reads -- an arrive
+  // per gather warp (of both CTAs when paired) plus the TMA thread's
+  // arrive.expect_tx, whose byte count covers the weight tile (NSPLIT: and
+  // the other CTA's copied A rows).  The MMA thread waits on a single
+  // barrier per stage: each wait it makes is a bubble in the tensor pipe.
   const uint32_t bar_full = sbase + L::kBar;
-  const uint32_t bar_wfull = bar_full + STAGES * 8;
-  const uint32_t bar_empty = bar_wfull + STAGES * 8;    // stage consumed (tcgen05.commit)
+  const uint32_t bar_empty = bar_full + STAGES * 8;     // stage consumed (tcgen05.commit)
   const uint32_t bar_tmem = bar_empty + STAGES * 8;
   uint32_t *s_tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kMisc);
   volatile int *s_abort = reinterpret_cast<volatile int *>(smem + L::kMisc + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  using R = Roles<iso_roles(MODE)>;
+  const bool gather_warp = R::gather(warp);
+  const int gw = R::gather_index(warp);      // gather warp index 0..15
   const uint32_t cr = CLUSTER ? ptx::cluster_ctarank() : 0u;   // rank in the CTA pair
   const bool leader = cr == 0;
   const int tile = CLUSTER ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
@@ -280,9 +331,8 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      // one arrive per gather warp (of both CTAs when paired)
-      ptx::mbar_init(bar_full + 8 * s, PAIR ? 2 * kGatherWarps : kGatherWarps);
-      ptx::mbar_init(bar_wfull + 8 * s, 1);                // TMA arrive + transaction bytes
+      // gather warps (of both CTAs when paired) + the TMA arrive with bytes
+      ptx::mbar_init(bar_full + 8 * s, (PAIR ? 2 : 1) * warps_per_stage<MODE, VB>() + 1);
       ptx::mbar_init(bar_empty + 8 * s, NSPLIT ? 2 : 1);   // tcgen05.commit (of both CTAs)
     }
     ptx::mbar_init(bar_tmem, 1);
@@ -292,7 +342,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   // Clustered CTAs: every barrier of both CTAs is initialised before any
   // cross-CTA arrive or copy can target it.
   if constexpr (CLUSTER) ptx::cluster_sync();
-  if (warp == kMmaWarp) {
+  if (warp == R::kMma) {
     if constexpr (PAIR) {
       ptx::tmem_alloc_pair(ptx::smem_u32(s_tmem_slot), BN);
       ptx::tmem_relinquish_pair();
@@ -301,21 +351,21 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
       ptx::tmem_relinquish();
     }
   }
-  if (warp == kTmaWarp && lane == 0) ptx::tma_prefetch_desc(&tmap_w);
+  if (warp == R::kTma && lane == 0) ptx::tma_prefetch_desc(&tmap_w);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *s_tmem_slot;
   // Barriers the gather warps and TMA copies report to: the leader's.
   const uint32_t full_dst = PAIR ? ptx::mapa_shared(bar_full, 0) : bar_full;
-  const uint32_t wfull_dst = PAIR ? ptx::mapa_shared(bar_wfull, 0) : bar_wfull;
   auto wait = [&](uint32_t bar, uint32_t parity, unsigned int site) -> bool {
     return ptx::mbar_wait_bounded(bar, parity, s_abort, &g_bevk_watchdog, site);
   };
 
-  if (warp < kGatherWarps) {
+  bool ok = true;
+  if (gather_warp) {
     // ---------------------------------------------------------- geometry
-    for (int e = threadIdx.x; e < p.T * kGRows; e += kGatherWarps * 32) {
+    for (int e = gw * 32 + lane; e < p.T * kGRows; e += kGatherWarps * 32) {
       const int t = e / kGRows, r = e - (e / kGRows) * kGRows;
       int packed;
       uint2 wh;
@@ -327,28 +377,37 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
 
     // ---------------------------------------------------------- gather
     // Each lane owns one VB-byte vector (VB/2 channels) of a 128-byte tile
-    // row: kLanesPerRow lanes cover a row, one warp instruction covers
-    // kRowsPerInstr rows, and each thread owns kRowsPerThr rows of every
-    // stage.  The four corner loads of all its rows for stage k+1 are issued
-    // (into registers) before stage k is interpolated and stored, so a full
-    // stage of corner reads is always in flight per thread.  A corner outside
-    // the image reads the zero line instead, so every load is unconditional
-    // and exact (no weight-times-garbage).  Stage coordinates advance
-    // incrementally (no integer division in the loop).
+    // row: kLanesPerRow lanes cover a row and one warp instruction covers
+    // kRowsPerInstr rows.  kWarpsPerStage warps build a stage (each thread
+    // owning kRowsPerThr rows of it); when that is fewer than the gather
+    // warps, the warps form kGroups groups that take stages in turn (group g:
+    // stages g, g + kGroups, ...).  The gather warps are issue-bound, so
+    // 32-byte vectors -- half the address and predicate work per byte --
+    // are worth the grouping.  The four corner loads of all its rows for a
+    // warp's next stage are issued (into registers) before its current stage
+    // is interpolated and stored, so a stage of corner reads is always in
+    // flight per thread.  Stage coordinates advance incrementally (no
+    // integer division in the loop).
     constexpr int kLanesPerRow = 128 / VB;
     constexpr int kRowsPerInstr = 32 / kLanesPerRow;
-    constexpr int kRowStride = kGatherWarps * kRowsPerInstr;  // between a thread's rows
+    constexpr int kWarpsPerStage = warps_per_stage<MODE, VB>();
+    constexpr int kGroups = kGatherWarps / kWarpsPerStage;
+    constexpr int kRowStride = kWarpsPerStage * kRowsPerInstr;  // between a thread's rows
     constexpr int kRowsPerThr = kGRows / kRowStride;
-    static_assert(kRowsPerThr >= 1 && kGRows % kRowStride == 0, "gather lane layout");
+    static_assert(kRowsPerThr >= 1 && kGRows % kRowStride == 0 &&
+                      kGroups * kWarpsPerStage == kGatherWarps && kGroups <= STAGES,
+                  "gather lane layout");
     constexpr int kWords = VB / 4;
     using Vec = ptx::Words<kWords>;
+    const int grp = gw / kWarpsPerStage;        // stage group of this warp
+    const int gi = gw - grp * kWarpsPerStage;   // warp index within the group
     const int j = lane % kLanesPerRow;
-    const int row0 = warp * kRowsPerInstr + lane / kLanesPerRow;
+    const int row0 = gi * kRowsPerInstr + lane / kLanesPerRow;
     const int xs2 = p.xs2, xs3 = p.xs3;
     const T *zline = reinterpret_cast<const T *>(g_dcn_zero_line) + j * (VB / 2);
-    // NSPLIT: the other CTA's A stages and B-full barriers
+    // NSPLIT: the other CTA's A stages and full barriers
     const uint32_t peer_sA = NSPLIT ? ptx::mapa_shared(sA, cr ^ 1u) : 0u;
-    const uint32_t peer_wfull = NSPLIT ? ptx::mapa_shared(bar_wfull, cr ^ 1u) : 0u;
+    const uint32_t peer_full = NSPLIT ? ptx::mapa_shared(bar_full, cr ^ 1u) : 0u;
     struct Prefetch {
       Vec v[kRowsPerThr][4];
       int ebase;  // geometry index of the prefetched stage's first row
@@ -358,10 +417,12 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
       int t, cc;
     };
     auto next_coord = [&](StageCoord c) {
-      if (++c.t == p.T) {
-        c.t = 0;
-        ++c.cc;
-      }
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g)
+        if (++c.t == p.T) {
+          c.t = 0;
+          ++c.cc;
+        }
       return c;
     };
     auto issue = [&](StageCoord sc, Prefetch &P) {
@@ -388,7 +449,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
         }
       }
     };
-    int cs = 0;          // stage slot of the stage being consumed
+    int cs = grp;        // stage slot of the stage being consumed (grp < STAGES)
     uint32_t cph = 0;    // its phase
     auto consume = [&](Prefetch &P) -> bool {
       // keep this stage's arithmetic behind the next stage's corner loads
@@ -423,36 +484,103 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
 #pragma unroll
           for (int i = 0; i < kRowsPerThr; ++i) {
             const uint32_t off_a = static_cast<uint32_t>(
-                (g_row0 + warp * kRowsPerInstr + i * kRowStride) * 128);
+                (g_row0 + gi * kRowsPerInstr + i * kRowStride) * 128);
             ptx::bulk_copy_smem_to_cluster(peer_sA + cs * L::kABytes + off_a,
                                            a_stage + off_a, kRowsPerInstr * 128,
-                                           peer_wfull + 8 * cs);
+                                           peer_full + 8 * cs);
           }
         }
         if constexpr (PAIR) ptx::mbar_arrive_cluster(full_dst + 8 * cs);
         else ptx::mbar_arrive(bar_full + 8 * cs);
       }
-      if (++cs == STAGES) { cs = 0; cph ^= 1; }
+      cs += kGroups;
+      if (cs >= STAGES) { cs -= STAGES; cph ^= 1; }
       return true;
     };
-    bool ok = true;
     {
       Prefetch A, B;
       StageCoord sc{0, 0};
-      if (p.n_k > 0) issue(sc, A);
-      for (int kit = 0; kit < p.n_k; kit += 2) {
+      for (int g = 0; g < grp; ++g)
+        if (++sc.t == p.T) { sc.t = 0; ++sc.cc; }
+      if (grp < p.n_k) issue(sc, A);
+      for (int kit = grp; kit < p.n_k; kit += 2 * kGroups) {
         sc = next_coord(sc);
-        if (kit + 1 < p.n_k) issue(sc, B);
+        if (kit + kGroups < p.n_k) issue(sc, B);
         ok = consume(A);
-        if (!ok || kit + 1 >= p.n_k) break;
+        if (!ok || kit + kGroups >= p.n_k) break;
         sc = next_coord(sc);
-        if (kit + 2 < p.n_k) issue(sc, A);
+        if (kit + 2 * kGroups < p.n_k) issue(sc, A);
         ok = consume(B);
         if (!ok) break;
       }
     }
+  } else if (warp == R::kTma) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kit = 0; kit < p.n_k; ++kit) {
+        const int s = kit % STAGES;
+        const uint32_t ph = (kit / STAGES) & 1;
+        if (!wait(bar_empty + 8 * s, ph ^ 1, kSiteTmaEmpty)) break;
+        const int t = kit % p.T;
+        const int cc = kit / p.T;
+        if constexpr (PAIR) {
+          // the leader expects both CTAs' halves on its own barrier
+          if (leader) ptx::mbar_arrive_expect_tx(bar_full + 8 * s, 2 * L::kBBytes);
+          ptx::tma_load_2d_pair(sB + s * L::kBBytes, &tmap_w, full_dst + 8 * s,
+                                t * p.Cin_pad + cc * kBK, n0 + static_cast<int>(cr) * L::kBRows);
+        } else {
+          // NSPLIT: the other CTA's A rows land on the same barrier
+          ptx::mbar_arrive_expect_tx(bar_full + 8 * s, L::kBBytes + (NSPLIT ? kGBytes : 0u));
+          ptx::tma_load_2d(sB + s * L::kBBytes, &tmap_w, bar_full + 8 * s,
+                           t * p.Cin_pad + cc * kBK, n0);
+        }
+        issued = kit + 1;
+      }
+      if (*s_abort && issued > 0) {
+        // The copies issued here (and, clustered, the ones reporting to the
+        // other CTA) share their barriers with gather arrivals that an abort
+        // may have skipped, so no barrier phase is left to wait on: give
+        // them time to land before shared memory can be released.
+        for (int i = 0; i < 64; ++i) __nanosleep(2000);
+      }
+    }
+  } else if (warp == R::kMma) {  // (the leader's, when paired)
+    if (lane == 0 && (leader || !PAIR)) {
+      constexpr uint32_t idesc = ptx::umma_idesc_f16(GM::kFmt, PAIR ? 2 * kBM : kBM, BN);
+      for (int kit = 0; kit < p.n_k; ++kit) {
+        const int s = kit % STAGES;
+        if (!wait(bar_full + 8 * s, (kit / STAGES) & 1, kSiteMmaFull)) break;
+        ptx::tc_fence_after();
+        const uint32_t a_stage = sA + s * L::kABytes;
+        const uint32_t b_stage = sB + s * L::kBBytes;
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          const uint64_t ad = ptx::umma_desc_sw128(a_stage + k * 32);
+          const uint64_t bd = ptx::umma_desc_sw128(b_stage + k * 32);
+          if constexpr (PAIR) ptx::umma_f16_ss_pair(tmem_base, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
+          else ptx::umma_f16_ss(tmem_base, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
+        }
+        if constexpr (PAIR) ptx::umma_commit_pair_both(bar_empty + 8 * s, 0x3);
+        else if constexpr (NSPLIT) ptx::umma_commit_multicast(bar_empty + 8 * s, 0x3);
+        else ptx::umma_commit(bar_empty + 8 * s);
+      }
+      // Tracks completion of every MMA issued above (also on abort, so the
+      // accumulator is quiescent before TMEM is released).
+      if constexpr (PAIR) ptx::umma_commit_pair_both(bar_tmem, 0x3);
+      else ptx::umma_commit(bar_tmem);
+      if (*s_abort) {
+        volatile int dummy = 0;
+        ptx::mbar_wait_bounded(bar_tmem, 0, &dummy, &g_bevk_watchdog, kSiteEpilogue);
+      }
+    }
+    __syncwarp();
+  }
 
-    // ---------------------------------------------------------- epilogue
+  // ------------------------------------------------------------ epilogue
+  // Warps 0-15 (gather, TMA, MMA and idle warps alike) drain TMEM: warp w
+  // reads lane quadrant w % 4, columns of quarter w / 4.
+  __syncwarp();
+  if (warp < kEpilogueWarps) {
     if (ok) ok = wait(bar_tmem, 0, kSiteEpilogue);
     if (ok) {
       ptx::tc_fence_after();
@@ -508,72 +636,6 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
         }
       }
     }
-  } else if (warp == kTmaWarp) {
-    if (lane == 0) {
-      int issued = 0;
-      for (int kit = 0; kit < p.n_k; ++kit) {
-        const int s = kit % STAGES;
-        const uint32_t ph = (kit / STAGES) & 1;
-        if (!wait(bar_empty + 8 * s, ph ^ 1, kSiteTmaEmpty)) break;
-        const int t = kit % p.T;
-        const int cc = kit / p.T;
-        if constexpr (PAIR) {
-          // the leader expects both CTAs' halves on its own barrier
-          if (leader) ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, 2 * L::kBBytes);
-          ptx::tma_load_2d_pair(sB + s * L::kBBytes, &tmap_w, wfull_dst + 8 * s,
-                                t * p.Cin_pad + cc * kBK, n0 + static_cast<int>(cr) * L::kBRows);
-        } else {
-          // NSPLIT: the other CTA's A rows land on the same barrier
-          ptx::mbar_arrive_expect_tx(bar_wfull + 8 * s, L::kBBytes + (NSPLIT ? kGBytes : 0u));
-          ptx::tma_load_2d(sB + s * L::kBBytes, &tmap_w, bar_wfull + 8 * s,
-                           t * p.Cin_pad + cc * kBK, n0);
-        }
-        issued = kit + 1;
-      }
-      if (*s_abort && CLUSTER) {
-        // Copies may report to the other CTA's barriers; give those issued
-        // here time to land before shared memory can be released.
-        for (int i = 0; i < 64; ++i) __nanosleep(2000);
-      } else if (*s_abort) {
-        // Let this CTA's own copies land before its shared memory is released.
-        volatile int never = 0;
-        for (int kit = issued - STAGES < 0 ? 0 : issued - STAGES; kit < issued; ++kit)
-          ptx::mbar_wait_bounded(bar_wfull + 8 * (kit % STAGES), (kit / STAGES) & 1, &never,
-                                 &g_bevk_watchdog, kSiteTmaEmpty);
-      }
-    }
-  } else {  // MMA warp (the leader's, when paired)
-    if (lane == 0 && (leader || !PAIR)) {
-      constexpr uint32_t idesc = ptx::umma_idesc_f16(GM::kFmt, PAIR ? 2 * kBM : kBM, BN);
-      for (int kit = 0; kit < p.n_k; ++kit) {
-        const int s = kit % STAGES;
-        const uint32_t ph = (kit / STAGES) & 1;
-        if (!wait(bar_wfull + 8 * s, ph, kSiteMmaFull) || !wait(bar_full + 8 * s, ph, kSiteMmaFull))
-          break;
-        ptx::tc_fence_after();
-        const uint32_t a_stage = sA + s * L::kABytes;
-        const uint32_t b_stage = sB + s * L::kBBytes;
-#pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {
-          const uint64_t ad = ptx::umma_desc_sw128(a_stage + k * 32);
-          const uint64_t bd = ptx::umma_desc_sw128(b_stage + k * 32);
-          if constexpr (PAIR) ptx::umma_f16_ss_pair(tmem_base, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
-          else ptx::umma_f16_ss(tmem_base, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
-        }
-        if constexpr (PAIR) ptx::umma_commit_pair_both(bar_empty + 8 * s, 0x3);
-        else if constexpr (NSPLIT) ptx::umma_commit_multicast(bar_empty + 8 * s, 0x3);
-        else ptx::umma_commit(bar_empty + 8 * s);
-      }
-      // Tracks completion of every MMA issued above (also on abort, so the
-      // accumulator is quiescent before TMEM is released).
-      if constexpr (PAIR) ptx::umma_commit_pair_both(bar_tmem, 0x3);
-      else ptx::umma_commit(bar_tmem);
-      if (*s_abort) {
-        volatile int dummy = 0;
-        ptx::mbar_wait_bounded(bar_tmem, 0, &dummy, &g_bevk_watchdog, kSiteEpilogue);
-      }
-    }
-    __syncwarp();
   }
 
   ptx::tc_fence_before();
@@ -581,7 +643,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   // Clustered CTAs: neither leaves (or frees TMEM) while the other may still
   // be reading its accumulator, arriving on its barriers or copying into it.
   if constexpr (CLUSTER) ptx::cluster_sync();
-  if (warp == kMmaWarp) {
+  if (warp == R::kMma) {
     ptx::tc_fence_after();
     if constexpr (PAIR) ptx::tmem_dealloc_pair(tmem_base, BN);
     else ptx::tmem_dealloc(tmem_base, BN);
@@ -590,7 +652,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
 
 // VB = bytes of input channels one gather lane loads per corner (16 or 32).
 template <typename T, int BN, int STAGES, int VB>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(tc_threads<kModeSingle>(), 1)
 dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
                   const T *__restrict__ x, const T *__restrict__ off, const T *__restrict__ msk,
                   const T *__restrict__ bias, T *__restrict__ y) {
@@ -598,7 +660,7 @@ dcn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
 }
 
 template <typename T, int BN, int STAGES, int VB>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc_threads<kModePair>(), 1)
 dcn_fwd_tc_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
                        const T *__restrict__ x, const T *__restrict__ off,
                        const T *__restrict__ msk, const T *__restrict__ bias,
@@ -607,7 +669,7 @@ dcn_fwd_tc_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParam
 }
 
 template <typename T, int BN, int STAGES, int VB>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc_threads<kModeNSplit>(), 1)
 dcn_fwd_tc_nsplit_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
                          const T *__restrict__ x, const T *__restrict__ off,
                          const T *__restrict__ msk, const T *__restrict__ bias,
@@ -664,7 +726,7 @@ int launch_tc(const TcParams &p, const CUtensorMap &tmap, const void *x, const v
   if (attr_err[dev] != cudaSuccess)
     return fail(BEVK_ERR_CUDA, "dcn tc: cudaFuncSetAttribute: %s",
                 cudaGetErrorString(attr_err[dev]));
-  kern<<<ctas, kThreads, L::kAlloc, stream>>>(tmap, p, static_cast<const T *>(x),
+  kern<<<ctas, tc_threads<MODE>(), L::kAlloc, stream>>>(tmap, p, static_cast<const T *>(x),
                                                static_cast<const T *>(off),
                                                static_cast<const T *>(msk),
                                                static_cast<const T *>(bias), static_cast<T *>(y));
@@ -742,7 +804,7 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
   // 32-byte corner loads when every pixel row starts on a 32-byte boundary
   // and a lane's 16 channels are all inside or all outside Cin (N-split CTAs
   // gather 64 rows: one 16-byte vector per lane covers them).
-  const bool v32 = mode != kModeNSplit && d.Cin % 16 == 0 && xs[0] % 16 == 0 &&
+  const bool v32 = d.Cin % 16 == 0 && xs[0] % 16 == 0 &&
                    xs[2] % 16 == 0 && xs[3] % 16 == 0 && aligned(x, 32);
   auto go = [&](auto tag) -> int {
     using T = typename decltype(tag)::type;
@@ -750,7 +812,8 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
     // stages keep shared memory at 159 KB, leaving ~92 KB of L1 for the
     // corner reads (four stages would leave ~28 KB and halve the hit rate).
     if (mode == kModeNSplit)
-      return launch_tc<T, 256, 3, kModeNSplit, 16>(p, tmap, x, off, msk, bias, y, nc, stream);
+      return v32 ? launch_tc<T, 256, 3, kModeNSplit, 32>(p, tmap, x, off, msk, bias, y, nc, stream)
+                 : launch_tc<T, 256, 3, kModeNSplit, 16>(p, tmap, x, off, msk, bias, y, nc, stream);
     if (v32) {
       if (BN == 256) return launch_tc<T, 256, 4, kModePair, 32>(p, tmap, x, off, msk, bias, y, nc, stream);
       if (BN == 128) return launch_tc<T, 128, 4, kModeSingle, 32>(p, tmap, x, off, msk, bias, y, nc, stream);
