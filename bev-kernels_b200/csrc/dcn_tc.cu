@@ -597,39 +597,92 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
       const bool vec_out = p.ys[1] == 1 && (p.Cout & 7) == 0 &&
                            (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (p.ys[0] & 7) == 0 &&
                            (p.ys[2] & 7) == 0 && (p.ys[3] & 7) == 0;
+      // A lane holds its own pixel's channels, so direct 16-byte stores put
+      // 32 pixels (32 lines) in every warp store.  When the warp's whole
+      // column range is in bounds and the output is channel-contiguous, its
+      // 32 x kColsPerWarp block is staged in shared memory (the A/B stage
+      // ring, free once the last MMA has completed) and written back row by
+      // row, kColsPerWarp * 2 contiguous bytes per row.
+      if (vec_out && n0 + (cgrp + 1) * kColsPerWarp <= p.Cout) {
+        constexpr int kCh = kColsPerWarp / 8;          // 16-byte chunks a row
+        const uint32_t blk = sA + static_cast<uint32_t>(warp * 32 * kCh * 16);
 #pragma unroll 1
-      for (int cb = 0; cb < kColsPerWarp; cb += kChunk) {
-        const int col = cgrp * kColsPerWarp + cb;
-        if (n0 + col >= p.Cout) break;
-        uint32_t r[kChunk];
-        ptx::tmem_ld_32x32b<kChunk>(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + col, r);
-        ptx::tmem_wait_ld();
-        if (m < p.M) {
+        for (int cb = 0; cb < kColsPerWarp; cb += kChunk) {
+          const int col = cgrp * kColsPerWarp + cb;
+          uint32_t r[kChunk];
+          ptx::tmem_ld_32x32b<kChunk>(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + col, r);
+          ptx::tmem_wait_ld();
           const int co0 = n0 + col;
-          float v[kChunk];
 #pragma unroll
-          for (int jj = 0; jj < kChunk; ++jj) {
-            v[jj] = __uint_as_float(r[jj]);
-            if (p.has_bias && co0 + jj < p.Cout) v[jj] += ld_float(bias + co0 + jj);
-            if (p.act_relu) v[jj] = fmaxf(v[jj], 0.f);
-          }
-          if (vec_out && co0 + kChunk <= p.Cout) {
+          for (int g = 0; g < kChunk / 8; ++g) {
+            uint4 pk;
+            uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
 #pragma unroll
-            for (int g = 0; g < kChunk / 8; ++g) {
-              uint4 pk;
-              uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
-#pragma unroll
-              for (int h = 0; h < 4; ++h)
-                pw[h] = static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h])) |
-                        (static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h + 1])) << 16);
-              *reinterpret_cast<uint4 *>(yrow + co0 + g * 8) = pk;
+            for (int h = 0; h < 4; ++h) {
+              float v0 = __uint_as_float(r[g * 8 + 2 * h]);
+              float v1 = __uint_as_float(r[g * 8 + 2 * h + 1]);
+              if (p.has_bias) {
+                v0 += ld_float(bias + co0 + g * 8 + 2 * h);
+                v1 += ld_float(bias + co0 + g * 8 + 2 * h + 1);
+              }
+              if (p.act_relu) {
+                v0 = fmaxf(v0, 0.f);
+                v1 = fmaxf(v1, 0.f);
+              }
+              pw[h] = static_cast<uint32_t>(GM::store_bits(v0)) |
+                      (static_cast<uint32_t>(GM::store_bits(v1)) << 16);
             }
-          } else {
+            const int c = cb / 8 + g;
+            ptx::st_shared_v4(blk + lane * (kCh * 16) + ((c ^ (lane % kCh)) << 4), pk);
+          }
+        }
+        __syncwarp();
+        constexpr int kRowsPerStore = 32 / kCh;
+        const int c = lane % kCh;
+        const uint64_t yrow_bits = reinterpret_cast<uint64_t>(yrow);
+#pragma unroll
+        for (int i = 0; i < 32 / kRowsPerStore; ++i) {
+          const int rl = i * kRowsPerStore + lane / kCh;   // row of the warp's block
+          const uint4 v = ptx::ld_shared_v4(blk + rl * (kCh * 16) + ((c ^ (rl % kCh)) << 4));
+          T *yr = reinterpret_cast<T *>(__shfl_sync(0xffffffffu, yrow_bits, rl));
+          if (m0 + q * 32 + rl < p.M)
+            *reinterpret_cast<uint4 *>(yr + n0 + cgrp * kColsPerWarp + c * 8) = v;
+        }
+      } else {
+#pragma unroll 1
+        for (int cb = 0; cb < kColsPerWarp; cb += kChunk) {
+          const int col = cgrp * kColsPerWarp + cb;
+          if (n0 + col >= p.Cout) break;
+          uint32_t r[kChunk];
+          ptx::tmem_ld_32x32b<kChunk>(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + col, r);
+          ptx::tmem_wait_ld();
+          if (m < p.M) {
+            const int co0 = n0 + col;
+            float v[kChunk];
 #pragma unroll
             for (int jj = 0; jj < kChunk; ++jj) {
-              if (co0 + jj < p.Cout) {
-                const uint16_t bits = GM::store_bits(v[jj]);
-                *reinterpret_cast<uint16_t *>(yrow + (co0 + jj) * p.ys[1]) = bits;
+              v[jj] = __uint_as_float(r[jj]);
+              if (p.has_bias && co0 + jj < p.Cout) v[jj] += ld_float(bias + co0 + jj);
+              if (p.act_relu) v[jj] = fmaxf(v[jj], 0.f);
+            }
+            if (vec_out && co0 + kChunk <= p.Cout) {
+#pragma unroll
+              for (int g = 0; g < kChunk / 8; ++g) {
+                uint4 pk;
+                uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
+#pragma unroll
+                for (int h = 0; h < 4; ++h)
+                  pw[h] = static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h])) |
+                          (static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h + 1])) << 16);
+                *reinterpret_cast<uint4 *>(yrow + co0 + g * 8) = pk;
+              }
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < kChunk; ++jj) {
+                if (co0 + jj < p.Cout) {
+                  const uint16_t bits = GM::store_bits(v[jj]);
+                  *reinterpret_cast<uint16_t *>(yrow + (co0 + jj) * p.ys[1]) = bits;
+                }
               }
             }
           }
