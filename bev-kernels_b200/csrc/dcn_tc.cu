@@ -602,12 +602,16 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
       // A lane holds its own pixel's channels, so direct 16-byte stores put
       // 32 pixels (32 lines) in every warp store.  When the warp's whole
       // column range is in bounds and the output is channel-contiguous, its
-      // 32 x kColsPerWarp block is staged in shared memory (the A/B stage
-      // ring, free once the last MMA has completed) and written back row by
-      // row, kColsPerWarp * 2 contiguous bytes per row.
+      // 32 x kColsPerWarp block is staged in shared memory and written back
+      // row by row, kColsPerWarp * 2 contiguous bytes per row.
       if (vec_out && n0 + (cgrp + 1) * kColsPerWarp <= p.Cout) {
         constexpr int kCh = kColsPerWarp / 8;          // 16-byte chunks a row
-        const uint32_t blk = sA + static_cast<uint32_t>(warp * 32 * kCh * 16);
+        // Staged in the weight ring: only this CTA's TMA writes it and the
+        // MMAs (also the partner's, in a pair) have finished reading it.  The
+        // A ring is not free yet under N-split: bulk copies to the other CTA
+        // may still be reading it.
+        static_assert(kEpilogueWarps * 32 * kCh * 16 <= STAGES * L::kBBytes, "staging space");
+        const uint32_t blk = sB + static_cast<uint32_t>(warp * 32 * kCh * 16);
 #pragma unroll 1
         for (int cb = 0; cb < kColsPerWarp; cb += kChunk) {
           const int col = cgrp * kColsPerWarp + cb;
