@@ -396,6 +396,9 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
     constexpr int kGroups = kGatherWarps / kWarpsPerStage;
     constexpr int kRowStride = kWarpsPerStage * kRowsPerInstr;  // between a thread's rows
     constexpr int kRowsPerThr = kGRows / kRowStride;
+    // A gather warp waits for its stage's slot with a parity wait, which
+    // tells two adjacent phases of the slot's barrier apart and no more: a
+    // group's next stage may be at most STAGES stages ahead of its last one.
     static_assert(kRowsPerThr >= 1 && kGRows % kRowStride == 0 &&
                       kGroups * kWarpsPerStage == kGatherWarps && kGroups <= STAGES,
                   "gather lane layout");
