@@ -315,6 +315,45 @@ def bench_dcn(cfg_name, steps, warmup, device, seed, img0, stream, dist=None, cl
                 sets=sets)
 
 
+def bench_dcn_pack(cfg_name, steps, warmup, device, seed, stream, fused):
+    """The Pack module's forward as BEVFormer calls it (DCNSplitNHWCFunction:
+    offset conv -> sigmoid mask -> DCN -> FrozenBN + ReLU), NHWC.  fused=False
+    runs the offset conv on cuDNN (the reference's structure,
+    dcn_split_nhwc.py:171-205); fused=True runs its channel reduction as one
+    GEMM with fp32 output and the tap sum in this library's kernel.  Either
+    way its output feeds the fused DCN kernel (sigmoid on load, BN folded,
+    ReLU in the epilogue).  Offset-conv weights are scaled so that the
+    offsets have a standard deviation of 2 px, as in the BASELINE configs."""
+    import torch
+    from modulated_deform_conv.dcn_split_nhwc import _forward_nhwc
+    cfg = DCN_CFGS[cfg_name]
+    dt = getattr(torch, cfg["dtype"])
+    B, C, H, W, Co = cfg["B"], cfg["C"], cfg["H"], cfg["W"], cfg["Cout"]
+    flops, nbytes = dcn_work(cfg)
+    flops += 2 * B * H * W * 27 * C * 9
+    sets = []
+    for i in range(n_sets_for(nbytes)):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 31 + i)
+        x = torch.randn(B, H, W, C, generator=g, device=device).to(dt)
+        w_off = (torch.randn(27, C, 3, 3, generator=g, device=device) *
+                 (2.0 / math.sqrt(9 * C))).to(dt)
+        b_off = torch.zeros(27, device=device, dtype=dt)
+        w = (torch.randn(Co, C, 3, 3, generator=g, device=device) *
+             math.sqrt(2.0 / (C * 9))).to(dt)
+        scale = torch.rand(Co, generator=g, device=device) + 0.5
+        shift = torch.randn(Co, generator=g, device=device) * 0.1
+        sets.append((x, w_off, b_off, w, scale, shift))
+
+    def make(s):
+        x, w_off, b_off, w, scale, shift = s
+        return lambda: _forward_nhwc(x, w_off, b_off, w, None, 1, 1, 1, scale, shift, True,
+                                     gemm_offset=fused)
+
+    ms = graph_time([make(s) for s in sets], steps, warmup, stream)
+    return dict(ms=ms, flops=flops, per_launch_s=ms / 1e3 / steps, n_sets=len(sets))
+
+
 def bench_dcn_bwd(cfg_name, steps, warmup, device, seed, stream):
     """DCN backward as autograd runs it: dO . W^T (GEMM), the col2im scatter
     into grad_input / grad_offset / grad_mask, the im2col gather and
@@ -537,7 +576,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--only", choices=("cfg2", "cfg3", "cfg4", "cfg5", "bwd_cfg2", "bwd_cfg3",
-                                       "bwd_cfg4", "bwd_cfg5"),
+                                       "bwd_cfg4", "bwd_cfg5", "pack_cfg2", "pack_cfg3"),
                     help="time one workload's kernel only (profiling runs: no e2e, "
                          "secondary or CPU legs; prints a reduced line)")
     args = ap.parse_args()
@@ -571,6 +610,12 @@ def main():
             r = bench_dcn(args.only, args.steps, args.warmup, device, seed, 0, stream, dist)
             del r["sets"]
             extra = {"tflops": r["flops"] / r["per_launch_s"] / 1e12}
+        elif args.only.startswith("pack_"):
+            r = bench_dcn_pack(args.only[5:], args.steps, args.warmup, device, seed, stream, True)
+            r0 = bench_dcn_pack(args.only[5:], args.steps, args.warmup, device, seed, stream,
+                                False)
+            extra = {"tflops": r["flops"] / r["per_launch_s"] / 1e12,
+                     "cudnn_offset_conv_us_per_call": r0["per_launch_s"] * 1e6}
         elif args.only in ("bwd_cfg2", "bwd_cfg3"):
             r = bench_dcn_bwd(args.only[4:], args.steps, args.warmup, device, seed, stream)
             extra = {"tflops": r["flops"] / r["per_launch_s"] / 1e12}
@@ -631,6 +676,19 @@ def main():
                 "roofline_us": r["bytes"] / (peaks["hbm_gbs"] * 1e9) * 1e6,
                 "traffic": _traffic(f"msda_fwd {name}")}
             torch.cuda.empty_cache()
+        for name in ("cfg2", "cfg3"):
+            for fused in (False, True):
+                r = bench_dcn_pack(name, min(k2, 200), args.warmup, device, seed + 5, stream,
+                                   fused)
+                a = r["flops"] / r["per_launch_s"] / 1e12
+                how = ("offset conv as one GEMM (fp32 out) + tap-sum kernel"
+                       if fused else "offset conv on cuDNN")
+                secondary[f"dcn_pack_{name}_{'gemm' if fused else 'cudnn'}"] = {
+                    "workload": DCN_CFGS[name]["desc"].replace(" fwd", " Pack fwd") +
+                                f" with FrozenBN+ReLU; {how}",
+                    "us_per_call": r["per_launch_s"] * 1e6, "tflops": a,
+                    "frac_tensor_peak": a / peaks["bf16_tflops"]}
+                torch.cuda.empty_cache()
         for name in ("cfg2", "cfg3"):
             r = bench_dcn_bwd(name, min(k2, 100), args.warmup, device, seed + 4, stream)
             a = r["flops"] / r["per_launch_s"] / 1e12

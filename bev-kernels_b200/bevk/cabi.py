@@ -37,6 +37,8 @@ EXPORTED_SYMBOLS = (
     "bevk_dcn_pack_weight",
     "bevk_dcn_forward_workspace_bytes",
     "bevk_dcn_forward",
+    "bevk_dcn_offset_conv_sum",
+    "bevk_dcn_forward_zoff",
     "bevk_dcn_forward_noalloc",
     "bevk_modulated_deformable_im2col",
     "bevk_modulated_deformable_im2col_opt",
@@ -47,6 +49,13 @@ EXPORTED_SYMBOLS = (
     "bevk_ms_deform_attn_backward_workspace_bytes",
     "bevk_ms_deform_attn_backward",
 )
+
+
+class DcnZoffArgs(ctypes.Structure):
+    """Mirror of ``bevk_dcn_zoff_args``."""
+
+    _fields_ = [("partials", ctypes.c_void_p), ("partials_ld", ctypes.c_int64),
+                ("offset_bias", ctypes.c_void_p), ("offset_out", ctypes.c_void_p)]
 
 
 class DcnProblem(ctypes.Structure):
@@ -121,6 +130,10 @@ def lib():
     L.bevk_dcn_forward.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp, sz, vp]
     L.bevk_dcn_forward_noalloc.restype = i
     L.bevk_dcn_forward_noalloc.argtypes = [pp, vp, vp, vp, vp, vp, vp, vp]
+    L.bevk_dcn_offset_conv_sum.restype = i
+    L.bevk_dcn_offset_conv_sum.argtypes = [pp, ctypes.POINTER(DcnZoffArgs), vp]
+    L.bevk_dcn_forward_zoff.restype = i
+    L.bevk_dcn_forward_zoff.argtypes = [pp, ctypes.POINTER(DcnZoffArgs), vp, vp, vp, vp, vp]
     L.bevk_dcn_columns.restype = i
     L.bevk_dcn_columns.argtypes = [pp, vp, vp, vp, vp, i, vp]
     L.bevk_dcn_col2im.restype = i

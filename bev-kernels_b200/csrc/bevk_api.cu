@@ -194,6 +194,40 @@ BEVK_API size_t bevk_dcn_forward_workspace_bytes(const bevk_dcn_problem *p) {
   return static_cast<size_t>(d.B) * d.H * d.W * d.Cin * dtype_size(p->dtype);
 }
 
+BEVK_API int bevk_dcn_offset_conv_sum(const bevk_dcn_problem *p, const bevk_dcn_zoff_args *z,
+                                      bevk_stream_t stream) {
+  clear_error();
+  DcnDims d;
+  int st = dcn_dims(p, &d);
+  if (st != BEVK_OK) return st;
+  if (!z || !z->partials || !z->offset_out)
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "dcn_offset_conv_sum: null pointer");
+  if (z->partials_ld < 3 * d.T * d.T)
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "dcn_offset_conv_sum: partials_ld %lld < 3*T*T",
+                static_cast<long long>(z->partials_ld));
+  return launch_dcn_offset_sum(p, d, z->partials, z->partials_ld, z->offset_bias, z->offset_out,
+                               reinterpret_cast<cudaStream_t>(stream));
+}
+
+BEVK_API int bevk_dcn_forward_zoff(const bevk_dcn_problem *p, const bevk_dcn_zoff_args *z,
+                                   const void *input, const void *packed_weight,
+                                   const void *bias, void *output, bevk_stream_t stream) {
+  int st = bevk_dcn_offset_conv_sum(p, z, stream);
+  if (st != BEVK_OK) return st;
+  DcnDims d;
+  dcn_dims(p, &d);
+  // offset / mask views of the [B, Ho, Wo, 3T] offset-conv output
+  bevk_dcn_problem q = *p;
+  const int64_t c3 = 3 * d.T;
+  const int64_t ys[4] = {static_cast<int64_t>(d.Ho) * d.Wo * c3, 1,
+                         static_cast<int64_t>(d.Wo) * c3, c3};
+  for (int i = 0; i < 4; ++i) q.offset_strides[i] = q.mask_strides[i] = ys[i];
+  q.mask_is_logit = 1;
+  const char *yb = static_cast<const char *>(z->offset_out);
+  return bevk_dcn_forward(&q, input, yb, yb + 2 * d.T * dtype_size(p->dtype), packed_weight, bias,
+                          output, nullptr, 0, stream);
+}
+
 BEVK_API int bevk_dcn_forward(const bevk_dcn_problem *p, const void *input, const void *offset,
                               const void *mask, const void *packed_weight, const void *bias,
                               void *output, void *workspace, size_t workspace_bytes,

@@ -87,6 +87,12 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *p, const DcnDims &d,
                           const void *off, const void *msk, const void *wpk,
                           const void *bias, void *out, cudaStream_t stream);
 
+// Offset convolution from its per-tap partial products (see
+// bevk_dcn_zoff_args): y[m, c] = round(bias[c] + sum_t z[p_t(m) * ld + t*3T + c]),
+// y [B*Ho*Wo][3T] in the problem dtype (fp16/bf16/fp32).
+int launch_dcn_offset_sum(const bevk_dcn_problem *p, const DcnDims &d, const float *z,
+                          int64_t ld, const float *bias, void *y, cudaStream_t stream);
+
 // Column-matrix ops.  col_layout 0: [C*T, B*Ho*Wo] (row c*T + t);
 // col_layout 1: [B*Ho*Wo, T*C] (k = t*C + c).
 int launch_dcn_im2col(const bevk_dcn_problem *p, const DcnDims &d, const void *x,

@@ -142,6 +142,51 @@ Tensor dcn_pack_weight(const Tensor &weight, int64_t groups) {
   return packed;
 }
 
+// Offset convolution from its per-tap partial products
+// (bevk_dcn_offset_conv_sum): partials [B*H*W, ld >= T*3T] fp32 with unit
+// column stride; offset_out [B, Ho, Wo, 3T] contiguous in the output dtype.
+void dcn_offset_conv_sum(const Tensor &partials, const c10::optional<Tensor> &offset_bias,
+                         Tensor offset_out, int64_t batch, int64_t height, int64_t width,
+                         int64_t kernel_h, int64_t kernel_w, int64_t stride_h, int64_t stride_w,
+                         int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w) {
+  check_cuda(partials, "partials");
+  check_same_device(partials, offset_out, "offset_out");
+  const int64_t T = kernel_h * kernel_w;
+  TORCH_CHECK(partials.scalar_type() == at::kFloat && partials.dim() == 2 &&
+                  partials.size(0) == batch * height * width && partials.size(1) >= T * 3 * T &&
+                  partials.stride(1) == 1 && partials.stride(0) >= T * 3 * T,
+              "bevk: partials must be fp32 [B*H*W, >= 3*T*T] with unit column stride");
+  Tensor ob;
+  if (offset_bias.has_value() && offset_bias->defined()) {
+    ob = offset_bias->to(at::kFloat).contiguous();
+    check_same_device(partials, ob, "offset_bias");
+    TORCH_CHECK(ob.numel() == 3 * T, "bevk: offset_bias must have 3*kH*kW elements");
+  }
+  bevk_dcn_problem p;
+  std::memset(&p, 0, sizeof(p));
+  p.dtype = dtype_of(offset_out);
+  p.batch = static_cast<int>(batch);
+  p.height = static_cast<int>(height);
+  p.width = static_cast<int>(width);
+  p.in_channels = 8;
+  p.out_channels = 1;
+  p.kernel_h = static_cast<int>(kernel_h); p.kernel_w = static_cast<int>(kernel_w);
+  p.stride_h = static_cast<int>(stride_h); p.stride_w = static_cast<int>(stride_w);
+  p.pad_h = static_cast<int>(pad_h); p.pad_w = static_cast<int>(pad_w);
+  p.dilation_h = static_cast<int>(dil_h); p.dilation_w = static_cast<int>(dil_w);
+  p.groups = 1; p.deformable_groups = 1;
+  int ho = 0, wo = 0;
+  check_status(bevk_dcn_output_size(&p, &ho, &wo), "dcn_offset_conv_sum");
+  TORCH_CHECK(offset_out.is_contiguous() && offset_out.dim() == 4 && offset_out.size(0) == batch &&
+                  offset_out.size(1) == ho && offset_out.size(2) == wo &&
+                  offset_out.size(3) == 3 * T,
+              "bevk: offset_out must be contiguous [B, Ho, Wo, 3*kH*kW]");
+  const c10::cuda::CUDAGuard guard(partials.device());
+  bevk_dcn_zoff_args z{partials.data_ptr<float>(), partials.stride(0),
+                       ob.defined() ? ob.data_ptr<float>() : nullptr, offset_out.data_ptr()};
+  check_status(bevk_dcn_offset_conv_sum(&p, &z, current_stream(partials)), "dcn_offset_conv_sum");
+}
+
 // Fused forward into a caller-provided output (any memory format).
 void dcn_forward(const Tensor &input, const Tensor &offset, const Tensor &mask,
                  const Tensor &packed_weight, const c10::optional<Tensor> &bias, Tensor output,
@@ -424,6 +469,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Modulated deformable gather, NHWC column matrix [B*Ho*Wo, kH*kW*C]");
   m.def("dcn_pack_weight", &dcn_pack_weight, "Pack [Cout, Cin/g, kH, kW] weights",
         py::arg("weight"), py::arg("groups") = 1);
+  m.def("dcn_offset_conv_sum", &dcn_offset_conv_sum,
+        "Offset convolution of the Pack module from its per-tap partial products",
+        py::arg("partials"), py::arg("offset_bias"), py::arg("offset_out"), py::arg("batch"),
+        py::arg("height"), py::arg("width"), py::arg("kernel_h"), py::arg("kernel_w"),
+        py::arg("stride_h"), py::arg("stride_w"), py::arg("pad_h"), py::arg("pad_w"),
+        py::arg("dil_h"), py::arg("dil_w"));
   m.def("dcn_forward", &dcn_forward, "Fused DCNv2 forward (tcgen05 / exact SIMT)",
         py::arg("input"), py::arg("offset"), py::arg("mask"), py::arg("packed_weight"),
         py::arg("bias"), py::arg("output"), py::arg("kernel_h"), py::arg("kernel_w"),

@@ -14,6 +14,8 @@ from .modulated_deform_conv import (  # noqa: F401
     ext_modulated_deformable_im2col,
     ext_modulated_deformable_im2col_opt,
     modulated_deform_conv2d,
+    offset_conv,
+    offset_conv_partials,
     packed_weight,
 )
 from .dcn_split_nhwc import (  # noqa: F401

@@ -173,6 +173,53 @@ def dcn_forward_into(input, offset, mask, weight, bias, output, stride, padding,
     return output
 
 
+def offset_conv_partials(x_nhwc, w_off):
+    """Per-tap partial products of the offset convolution, [B*H*W, ld] fp32
+    (ld = T*3T rounded up to a multiple of 32): row p, column t*3T + c holds
+    sum_ci x[p, ci] * w_off[c, ci, t] -- one GEMM with fp32 output, the
+    channel reduction of the Pack module's conv_offset
+    (dcn_split_nhwc.py:171-172).  Columns beyond T*3T are zero."""
+    B, H, W, Cin = x_nhwc.shape
+    return torch.mm(x_nhwc.reshape(B * H * W, Cin), _offset_gemm_weight(w_off, x_nhwc.dtype).t(),
+                    out_dtype=torch.float32)
+
+
+def _offset_gemm_weight(w_off, dtype):
+    """w_off [3T, Cin, kH, kW] as the GEMM operand [ld, Cin] (row t*3T + c,
+    zero rows up to ld), cached on w_off like packed_weight."""
+    key = (w_off._version, dtype, w_off.device, tuple(w_off.shape))
+    cached = getattr(w_off, "_bevk_offset_gemm", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    c3, cin, kh, kw = w_off.shape
+    n = kh * kw * c3
+    wz = torch.zeros((n + 31) // 32 * 32, cin, device=w_off.device, dtype=dtype)
+    wz[:n] = w_off.detach().permute(2, 3, 0, 1).reshape(n, cin)
+    try:
+        w_off._bevk_offset_gemm = (key, wz)
+    except (AttributeError, RuntimeError):
+        pass
+    return wz
+
+
+def offset_conv(x_nhwc, w_off, b_off, stride, padding, dilation):
+    """The Pack module's offset convolution (dcn_split_nhwc.py:171-172) as
+    [B, Ho, Wo, 3T] in x's dtype: its channel reduction as one GEMM with fp32
+    output (offset_conv_partials), then the tap sum, bias and one rounding in
+    a kernel of this library (bevk_dcn_offset_conv_sum)."""
+    B, H, W, _ = x_nhwc.shape
+    c3, _, kh, kw = w_off.shape
+    sh, sw = _pair(stride)
+    ph, pw = _pair(padding)
+    dh, dw = _pair(dilation)
+    Ho = (H + 2 * ph - (dh * (kh - 1) + 1)) // sh + 1
+    Wo = (W + 2 * pw - (dw * (kw - 1) + 1)) // sw + 1
+    y = torch.empty(B, Ho, Wo, c3, device=x_nhwc.device, dtype=x_nhwc.dtype)
+    _load_ext().dcn_offset_conv_sum(offset_conv_partials(x_nhwc, w_off), b_off, y, B, H, W,
+                                    kh, kw, sh, sw, ph, pw, dh, dw)
+    return y
+
+
 # ---------------------------------------------------------------------------
 # autograd Function (reference: modulated_deform_conv.py:318-502)
 # ---------------------------------------------------------------------------

@@ -143,6 +143,55 @@ BEVK_API int bevk_dcn_forward(const bevk_dcn_problem *p, const void *input,
                               size_t workspace_bytes, bevk_stream_t stream);
 
 /*
+ * The offset convolution of the DCNv2 Pack module from its per-tap partial
+ * products.  T = kernel_h * kernel_w, P = batch * height * width (input pixels
+ * in NHWC order).
+ */
+typedef struct bevk_dcn_zoff_args {
+  const float *partials;     /* [P][partials_ld] fp32: partials[p*ld + t*3T + c]
+                                = sum_ci input[p, ci] * w_off[c, ci, t]        */
+  int64_t partials_ld;       /* row stride in elements, >= T * 3T             */
+  const float *offset_bias;  /* [3T] fp32 (the offset conv's bias) or NULL    */
+  void *offset_out;          /* [batch*Ho*Wo][3T] contiguous, problem dtype:
+                                the offset-conv output                        */
+} bevk_dcn_zoff_args;
+
+/*
+ * Offset convolution of the Pack module (conv_offset of
+ * DCNSplitNHWCFunction.forward, modulated_deform_conv/dcn_split_nhwc.py:171-172,
+ * and of ModulatedDeformConv2dPack, modulated_deform_conv.py:604-626): the
+ * DCN's kernel size, stride, padding and dilation, 3T output channels --
+ * channel c < 2T is offset channel c (2t = dh, 2t+1 = dw of tap t), channel
+ * 2T + t the mask logit of tap t.  The reference runs it as a cuDNN
+ * convolution; its fused offset-conv + gather kernel
+ * (csrc/dcn_fused_nhwc_kernel.cuh:211-303, bound at csrc/binding.cpp:167-169)
+ * and the TileLang mega-kernel (modulated_deform_conv/fused_tl.py:565-688)
+ * compute it in-kernel.
+ *
+ * Here its channel reduction is one plain GEMM the caller runs ([P, Cin] x
+ * [Cin, T*3T] with fp32 output: partials); this call adds the T shifted taps
+ * and offset_bias for every output pixel and rounds the sum to the problem
+ * dtype (what the unfused offset-conv output holds), writing offset_out.
+ * (Summing the taps in the DCN kernel's prologue instead measured slower on
+ * B200: the extra L2 round trips sit on every tile's critical path.)
+ * fp16, bf16 and fp32; kH*kW <= 9.  Only the shape, stride, padding,
+ * dilation and dtype fields of the problem are used.
+ */
+BEVK_API int bevk_dcn_offset_conv_sum(const bevk_dcn_problem *p, const bevk_dcn_zoff_args *z,
+                                      bevk_stream_t stream);
+
+/*
+ * bevk_dcn_offset_conv_sum followed by bevk_dcn_forward on its output (offsets
+ * from offset_out channels [0, 2T), the mask sigmoid applied on load to
+ * channels [2T, 3T)).  The problem's offset_strides, mask_strides and
+ * mask_is_logit are ignored; input must not need the NCHW copy of
+ * bevk_dcn_forward (no workspace is taken).
+ */
+BEVK_API int bevk_dcn_forward_zoff(const bevk_dcn_problem *p, const bevk_dcn_zoff_args *z,
+                                   const void *input, const void *packed_weight,
+                                   const void *bias, void *output, bevk_stream_t stream);
+
+/*
  * Allocation-free variant of bevk_dcn_forward.  No counterpart in the
  * reference: it exists for callers that cannot call cudaMalloc or hand out a
  * workspace at the moment they run the layer -- an inference engine's plugin
