@@ -115,7 +115,7 @@ class ClockSampler:
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
 
-    def __init__(self, device_index: int, period_s: float = 0.002):
+    def __init__(self, device_index: int, period_s: float = 0.0005):
         self.samples, self.reasons, self.max_mhz = [], set(), None
         self._stop = threading.Event()
         self._thread = None
@@ -146,13 +146,19 @@ class ClockSampler:
             try:
                 self._sample()
             except Exception:
+                self._ready.set()
                 return
+            self._ready.set()
             time.sleep(self._period)
 
     def __enter__(self):
         if self._nv is not None:
+            self._ready = threading.Event()
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
+            # the timed region starts only once the sampler is running, so a
+            # region of a few milliseconds still gets several samples
+            self._ready.wait(1.0)
         return self
 
     def __exit__(self, *exc):
