@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from .modulated_deform_conv import _load_ext, dcn_forward_into, offset_conv
+from .modulated_deform_conv import _load_ext, _tap_major_weight, dcn_forward_into, offset_conv
 
 
 def out_size(H, pad, dil, k, stride):
@@ -162,8 +162,8 @@ class DCNSplitNHWCFunction(torch.autograd.Function):
                 go = go * relu_mask.reshape(M, Cout)
             go = go * bn_scale.to(go.dtype).view(1, -1)
         dO = go.to(dt)
-        w_flat = weight.permute(2, 3, 1, 0).reshape(K, Cout).to(dt)      # [K, Cout], k = t*Cin + c
-        dcol = torch.mm(dO, w_flat.t())                                   # [M, K]
+        w_tap = _tap_major_weight(weight, dt)                             # [Cout, K], k = t*Cin + c
+        dcol = torch.mm(dO, w_tap)                                        # [M, K]
         y_nhwc = y.permute(0, 2, 3, 1).contiguous()                       # [B, Ho, Wo, 3T]
         gX = torch.zeros(B, H, W, Cin, device=x.device, dtype=torch.float32)
         gOff = torch.zeros(B, Ho, Wo, 2 * T, device=x.device, dtype=torch.float32)
@@ -172,9 +172,13 @@ class DCNSplitNHWCFunction(torch.autograd.Function):
             dcol, x.contiguous(), y_nhwc, y_nhwc, B, Cin, H, W, Ho, Wo, kH, kW, pd, pd, st, st,
             dl, dl, 1, gX, gOff, gMask)
         cols = gather_cols_nhwc(x, y_nhwc, None, kH, kW, st, pd, dl)      # [M, K]
-        grad_weight = torch.mm(cols.t().float(), dO.float()) \
+        # fp16/bf16 operands, fp32 products and accumulation: the reference's
+        # fp32 GEMM of the up-cast operands without the up-cast copies
+        gw32 = (torch.mm(cols.t(), dO, out_dtype=torch.float32)
+                if dt in (torch.float16, torch.bfloat16) else torch.mm(cols.t().float(), dO.float()))
+        grad_weight = gw32 \
             .view(kH, kW, Cin, Cout).permute(3, 2, 0, 1).contiguous().to(dt)
-        grad_bias = dO.float().sum(0).to(dt) if ctx.with_bias else None
+        grad_bias = dO.sum(0, dtype=torch.float32).to(dt) if ctx.with_bias else None
         # offset / mask convolution backward (regular convolution)
         dY = torch.cat([gOff, gMask], dim=-1).permute(0, 3, 1, 2).contiguous()   # [B, 3T, Ho, Wo]
         x_nchw = x.permute(0, 3, 1, 2).float()

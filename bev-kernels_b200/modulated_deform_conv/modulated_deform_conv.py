@@ -273,6 +273,22 @@ class ModulatedDeformConv2dFunction(Function):
         return grads + (None, None, None, None, None)
 
 
+def _tap_major_weight(weight, dtype):
+    """weight [Cout, Cg, kH, kW] as [Cout, kH*kW*Cg] (k = t*Cg + c) in dtype,
+    cached on the weight like packed_weight (the backward's dCol GEMM operand)."""
+    key = (weight._version, dtype, weight.device, tuple(weight.shape))
+    cached = getattr(weight, "_bevk_tap_major", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    cout, cg, kh, kw = weight.shape
+    wt = weight.detach().to(dtype).permute(0, 2, 3, 1).reshape(cout, kh * kw * cg).contiguous()
+    try:
+        weight._bevk_tap_major = (key, wt)
+    except (AttributeError, RuntimeError):
+        pass
+    return wt
+
+
 def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dilation,
                  groups=1, deform_groups=1, need_input=True, need_offset_mask=True,
                  need_weight=True, need_bias=True):
@@ -306,7 +322,7 @@ def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dila
     grad_input = grad_offset = grad_mask = grad_weight = grad_bias = None
     if need_input or need_offset_mask:
         # dcol[m, t*C + c] = sum_co dO[m, co] * weight[co, c_local, t]  (per conv group)
-        wt = weight.to(dt).permute(0, 2, 3, 1).reshape(G, Coutg, T * Cg)   # k = t*Cg + c
+        wt = _tap_major_weight(weight, dt).view(G, Coutg, T * Cg)          # k = t*Cg + c
         if G == 1:
             dcol = torch.mm(go, wt[0])
         else:
@@ -341,7 +357,7 @@ def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dila
             gw = gw.view(Cout, kH, kW, Cg).permute(0, 3, 1, 2)
         grad_weight = gw.contiguous().to(weight.dtype)
     if need_bias:
-        grad_bias = go.to(acc).sum(0).to(dt)
+        grad_bias = go.sum(0, dtype=acc).to(dt)
     return grad_input, grad_offset, grad_mask, grad_weight, grad_bias
 
 
