@@ -9,11 +9,15 @@ Parity status:
   * DCNv2 forward and backward: pinned against the reference's own PyTorch
     goldens through the fixtures in ``tests/golden`` (see
     ``tests/golden/make_golden.py``).
-  * MSDA: parity unpinned by an executable reference (MUSA-only upstream, no
-    golden vectors); restated from ``csrc_musa/msda/ms_deform_attn_kernels.cuh``
-    :7-49 and :559-623 (forward), :425-494 and :638-788 (backward) and
-    cross-checked against the independent grid_sample formulation in
-    ``oracle/msda_grid_sample.py`` (its torch autograd for the backward).
+  * MSDA forward: pinned against the reference's own generic forward kernel
+    (``csrc_musa/msda/ms_deform_attn_kernels.cuh:559-623`` with its bilinear
+    helper :7-49) compiled for the host from the reference tree with the
+    stand-ins in ``oracle/ref_shim`` (``reference_msda_forward``; built into
+    ``oracle/_ref`` by ``make -C oracle ref``), and cross-checked against the
+    independent grid_sample formulation in ``oracle/msda_grid_sample.py``.
+  * MSDA backward: restated from :425-494 and :638-788 and pinned only through
+    torch autograd of the grid_sample formulation (the reference's backward
+    kernels are warp- and block-cooperative and do not run single-threaded).
 
 All functions take and return numpy arrays (float32 compute; inputs of other
 float dtypes are up-cast, which is how fp16/bf16 kernel outputs are checked).
@@ -183,6 +187,39 @@ def msda_forward(value, spatial_shapes, level_start_index, sampling_loc, attn_we
                                      B, S, M, C, L, Q, P, _p(out), lo, hi, int(nthreads))
     if rc != 0:
         raise ValueError("oracle_msda_forward: invalid arguments")
+    return out
+
+
+_REF_PATH = os.path.join(_HERE, "_ref", "libmsda_ref.so")
+_REF_TREE = os.environ.get("BEVK_REFERENCE_DIR", "/root/reference")
+
+
+def reference_msda_available() -> bool:
+    """Whether the reference's own MSDA kernel is built for the host
+    (oracle/_ref, `make -C oracle ref`); built here on demand when the
+    reference tree is present."""
+    if not os.path.exists(_REF_PATH) and os.path.isdir(_REF_TREE):
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF_DIR={_REF_TREE}"], check=False)
+    return os.path.exists(_REF_PATH)
+
+
+def reference_msda_forward(value, spatial_shapes, level_start_index, sampling_loc,
+                           attn_weight):
+    """The reference's generic MSDA forward kernel
+    (csrc_musa/msda/ms_deform_attn_kernels.cuh:559-623) run on the host, fp32
+    -> [B, Q, heads*C]; the pin for msda_forward."""
+    lib = ctypes.CDLL(_REF_PATH)
+    value, loc, attn = _f32(value), _f32(sampling_loc), _f32(attn_weight)
+    shapes = np.ascontiguousarray(np.asarray(spatial_shapes, dtype=np.int64))
+    lsi = np.ascontiguousarray(np.asarray(level_start_index, dtype=np.int64))
+    B, S, M, C = value.shape
+    _, Q, _, L, P, _ = loc.shape
+    out = np.zeros((B, Q, M * C), np.float32)
+    rc = lib.ref_msda_forward_f32(_p(value), shapes.ctypes.data_as(_i64p),
+                                  lsi.ctypes.data_as(_i64p), _p(loc), _p(attn), B, S, M, C, L,
+                                  Q, P, _p(out))
+    if rc != 0:
+        raise ValueError("ref_msda_forward_f32: problem too large")
     return out
 
 

@@ -111,6 +111,38 @@ def test_msda_matches_grid_sample_random():
     assert oracle.rel_l2(got, want) <= 1e-6 and oracle.max_abs(got, want) <= 1e-5
 
 
+REF_MSDA_CASES = [
+    # B, level shapes, heads, C, Q, P, spread of locations beyond [0, 1]
+    (2, [(20, 30)], 8, 32, 300, 4, 0.1),
+    (3, [(23, 41), (12, 21), (6, 11), (3, 6)], 8, 32, 257, 8, 0.1),
+    (1, [(9, 7), (5, 4)], 4, 32, 100, 13, 0.2),
+    (2, [(10, 12), (5, 6)], 3, 24, 50, 3, 0.1),
+    (1, [(1, 1), (2, 1)], 8, 32, 40, 2, 0.3),       # degenerate levels
+    (1, [(29, 50), (15, 25)], 8, 32, 64, 8, 0.0),   # BEVFormer-like level shapes
+]
+
+
+@pytest.mark.parametrize("case", REF_MSDA_CASES, ids=[f"r{i}" for i in range(len(REF_MSDA_CASES))])
+def test_msda_matches_reference_kernel(case):
+    """The oracle's MSDA forward against the reference's own generic kernel
+    (ms_deform_attn_kernels.cuh:559-623) compiled for the host from the
+    reference tree (oracle/ref_msda.cpp, oracle/ref_shim)."""
+    if not oracle.reference_msda_available():
+        pytest.skip("reference tree not present and oracle/_ref not built")
+    B, shapes, M, C, Q, P, spread = case
+    rng = np.random.default_rng(len(shapes) * 100 + Q)
+    L = len(shapes)
+    sizes = [h * w for h, w in shapes]
+    lsi = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.int64)
+    value = rng.standard_normal((B, sum(sizes), M, C)).astype(np.float32)
+    loc = rng.uniform(-spread, 1 + spread, (B, Q, M, L, P, 2)).astype(np.float32)
+    attn = rng.random((B, Q, M, L, P)).astype(np.float32)
+    want = oracle.reference_msda_forward(value, np.array(shapes), lsi, loc, attn)
+    got = oracle.msda_forward(value, np.array(shapes), lsi, loc, attn)
+    # fp32 rounding only: the two builds contract multiply-adds differently
+    assert oracle.rel_l2(got, want) <= 1e-6 and oracle.max_abs(got, want) <= 1e-5
+
+
 def test_msda_boundary_coordinates():
     """Points exactly on the gates: h = -1 and h = H (dropped), h = H-1 (kept)."""
     H, W = 4, 5
