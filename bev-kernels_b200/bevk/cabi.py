@@ -45,6 +45,8 @@ EXPORTED_SYMBOLS = (
     "bevk_modulated_deformable_im2col_nhwc",
     "bevk_dcn_columns",
     "bevk_dcn_col2im",
+    "bevk_dcn_backward_data_workspace_bytes",
+    "bevk_dcn_backward_data",
     "bevk_ms_deform_attn_forward",
     "bevk_ms_deform_attn_backward_workspace_bytes",
     "bevk_ms_deform_attn_backward",
@@ -87,6 +89,20 @@ class DcnCol2imArgs(ctypes.Structure):
         ("problem", DcnProblem),
         ("col_dtype", ctypes.c_int),
         ("col_strides", ctypes.c_int64 * 3),
+        ("grad_input_strides", ctypes.c_int64 * 4),
+        ("grad_offset_strides", ctypes.c_int64 * 4),
+        ("grad_mask_strides", ctypes.c_int64 * 4),
+    ]
+
+
+class DcnBackwardDataArgs(ctypes.Structure):
+    """Mirror of ``bevk_dcn_backward_data_args``."""
+
+    _fields_ = [
+        ("problem", DcnProblem),
+        ("grad_dtype", ctypes.c_int),
+        ("dcol_ld", ctypes.c_int64),
+        ("col_ld", ctypes.c_int64),
         ("grad_input_strides", ctypes.c_int64 * 4),
         ("grad_offset_strides", ctypes.c_int64 * 4),
         ("grad_mask_strides", ctypes.c_int64 * 4),
@@ -138,6 +154,11 @@ def lib():
     L.bevk_dcn_columns.argtypes = [pp, vp, vp, vp, vp, i, vp]
     L.bevk_dcn_col2im.restype = i
     L.bevk_dcn_col2im.argtypes = [ctypes.POINTER(DcnCol2imArgs), vp, vp, vp, vp, vp, vp, vp, vp]
+    L.bevk_dcn_backward_data_workspace_bytes.restype = sz
+    L.bevk_dcn_backward_data_workspace_bytes.argtypes = [pp]
+    L.bevk_dcn_backward_data.restype = i
+    L.bevk_dcn_backward_data.argtypes = ([ctypes.POINTER(DcnBackwardDataArgs)] + [vp] * 9 +
+                                         [sz, vp])
     col_args = [vp, vp, vp] + [i] * 15
     L.bevk_modulated_deformable_im2col.restype = i
     L.bevk_modulated_deformable_im2col.argtypes = col_args + [vp, i, vp]

@@ -426,6 +426,42 @@ BEVK_API int bevk_dcn_col2im(const bevk_dcn_col2im_args *args, const void *input
                            grad_mask, reinterpret_cast<cudaStream_t>(stream));
 }
 
+BEVK_API size_t bevk_dcn_backward_data_workspace_bytes(const bevk_dcn_problem *p) {
+  if (!p) return 0;
+  bevk_dcn_problem pr = *p;
+  pr.out_channels = 1;
+  pr.groups = 1;
+  DcnDims d;
+  if (dcn_dims(&pr, &d) != BEVK_OK) return 0;
+  return dcn_backward_data_workspace_bytes(d);
+}
+
+BEVK_API int bevk_dcn_backward_data(const bevk_dcn_backward_data_args *args,
+                                    const void *input, const void *offset, const void *mask,
+                                    const void *dcol, void *grad_input, void *grad_offset,
+                                    void *grad_mask, void *col, void *workspace,
+                                    size_t workspace_bytes, bevk_stream_t stream) {
+  clear_error();
+  if (!args || !offset || !mask)
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "dcn_backward_data: null pointer");
+  if (!input && (grad_offset || grad_mask || col))
+    return fail(BEVK_ERR_INVALID_ARGUMENT,
+                "dcn_backward_data: grad_offset / grad_mask / col need the input");
+  if (!dcol && (grad_input || grad_offset || grad_mask))
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "dcn_backward_data: the gradients need dcol");
+  // out_channels and groups play no part in the data side
+  bevk_dcn_problem pr = args->problem;
+  pr.out_channels = 1;
+  pr.groups = 1;
+  DcnDims d;
+  const int st = dcn_dims(&pr, &d);
+  if (st != BEVK_OK) return st;
+  if (!grad_input && !grad_offset && !grad_mask && !col) return BEVK_OK;
+  return launch_dcn_backward_data(args, d, input, offset, mask, dcol, grad_input, grad_offset,
+                                  grad_mask, col, workspace, workspace_bytes,
+                                  reinterpret_cast<cudaStream_t>(stream));
+}
+
 BEVK_API size_t bevk_ms_deform_attn_backward_workspace_bytes(int batch, int spatial_size,
                                                              int num_heads, int channels,
                                                              int dtype) {

@@ -59,6 +59,12 @@ int dcn_dims(const bevk_dcn_problem *p, DcnDims *d);
 int launch_dcn_col2im(const bevk_dcn_col2im_args *a, const DcnDims &d, const void *input,
                       const void *offset, const void *mask, const void *dcol, void *grad_input,
                       void *grad_offset, void *grad_mask, cudaStream_t stream);
+size_t dcn_backward_data_workspace_bytes(const DcnDims &d);
+int launch_dcn_backward_data(const bevk_dcn_backward_data_args *a, const DcnDims &d,
+                             const void *input, const void *offset, const void *mask,
+                             const void *dcol, void *grad_input, void *grad_offset,
+                             void *grad_mask, void *col, void *workspace,
+                             size_t workspace_bytes, cudaStream_t stream);
 size_t msda_backward_workspace_bytes(int B, int S, int heads, int C, int dtype);
 int launch_msda_backward(const void *value, const int64_t *shapes, const int64_t *lsi,
                          const void *loc, const void *attn, const void *grad_out,

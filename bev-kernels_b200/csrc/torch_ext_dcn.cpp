@@ -423,6 +423,98 @@ void dcn_col2im(const Tensor &dcol, const c10::optional<Tensor> &input, const Te
                 gm.defined() ? &gm : nullptr, false, "dcn_col2im");
 }
 
+// Data side of the backward in one call (bevk_dcn_backward_data): NCHW-shaped
+// input / offset / mask / gradients in any memory format (an NHWC tensor is
+// passed as its permuted view), NHWC column matrices [M, kH*kW*C] with unit
+// column stride.  Returns false, having written nothing, when the layouts are
+// not the channel-contiguous 16-byte-vector ones the kernels need.
+bool dcn_backward_data(const c10::optional<Tensor> &dcol, const c10::optional<Tensor> &input,
+                       const Tensor &offset, const Tensor &mask, bool mask_is_logit,
+                       int64_t in_channels, int64_t height, int64_t width, int64_t kernel_h,
+                       int64_t kernel_w, int64_t stride_h, int64_t stride_w, int64_t pad_h,
+                       int64_t pad_w, int64_t dil_h, int64_t dil_w, int64_t deform_groups,
+                       c10::optional<Tensor> grad_input, c10::optional<Tensor> grad_offset,
+                       c10::optional<Tensor> grad_mask, c10::optional<Tensor> col) {
+  auto get = [](const c10::optional<Tensor> &t) {
+    return t.has_value() && t->defined() ? *t : Tensor();
+  };
+  const Tensor dc = get(dcol), in = get(input), gi = get(grad_input), go = get(grad_offset),
+               gm = get(grad_mask), cl = get(col);
+  check_cuda(offset, "offset");
+  check_same_device(offset, mask, "mask");
+  TORCH_CHECK(offset.dim() == 4 && mask.dim() == 4,
+              "bevk: dcn_backward_data: offset / mask must be 4-D");
+  TORCH_CHECK(mask.scalar_type() == offset.scalar_type(),
+              "bevk: dcn_backward_data: offset / mask must share a dtype");
+  for (const Tensor *t : {&dc, &in, &gi, &go, &gm, &cl})
+    if (t->defined()) check_same_device(offset, *t, "tensor");
+  for (const Tensor *t : {&dc, &in, &cl})
+    if (t->defined())
+      TORCH_CHECK(t->scalar_type() == offset.scalar_type(),
+                  "bevk: dcn_backward_data: input / dcol / col must have the offset dtype");
+  at::ScalarType gt = offset.scalar_type();
+  bool first = true;
+  for (const Tensor *t : {&gi, &go, &gm})
+    if (t->defined()) {
+      TORCH_CHECK(first || t->scalar_type() == gt,
+                  "bevk: dcn_backward_data: the gradients must share a dtype");
+      gt = t->scalar_type();
+      first = false;
+    }
+  const int64_t T = kernel_h * kernel_w;
+  const int64_t M = offset.size(0) * offset.size(2) * offset.size(3);
+  for (const Tensor *t : {&dc, &cl})
+    if (t->defined())
+      TORCH_CHECK(t->dim() == 2 && t->size(0) == M && t->size(1) == T * in_channels &&
+                      t->stride(1) == 1,
+                  "bevk: dcn_backward_data: column matrices must be [M, kH*kW*C] with unit "
+                  "column stride");
+  bevk_dcn_backward_data_args a;
+  std::memset(&a, 0, sizeof(a));
+  bevk_dcn_problem &p = a.problem;
+  p.dtype = dtype_of(offset);
+  p.batch = static_cast<int>(offset.size(0));
+  p.in_channels = static_cast<int>(in_channels);
+  p.height = static_cast<int>(height);
+  p.width = static_cast<int>(width);
+  p.out_channels = 1;
+  p.kernel_h = static_cast<int>(kernel_h); p.kernel_w = static_cast<int>(kernel_w);
+  p.stride_h = static_cast<int>(stride_h); p.stride_w = static_cast<int>(stride_w);
+  p.pad_h = static_cast<int>(pad_h); p.pad_w = static_cast<int>(pad_w);
+  p.dilation_h = static_cast<int>(dil_h); p.dilation_w = static_cast<int>(dil_w);
+  p.groups = 1;
+  p.deformable_groups = static_cast<int>(deform_groups);
+  p.mask_is_logit = mask_is_logit ? 1 : 0;
+  for (int i = 0; i < 4; ++i) {
+    p.input_strides[i] = in.defined() ? in.stride(i) : 0;
+    p.offset_strides[i] = offset.stride(i);
+    p.mask_strides[i] = mask.stride(i);
+    a.grad_input_strides[i] = gi.defined() ? gi.stride(i) : 0;
+    a.grad_offset_strides[i] = go.defined() ? go.stride(i) : 0;
+    a.grad_mask_strides[i] = gm.defined() ? gm.stride(i) : 0;
+  }
+  a.grad_dtype = first ? p.dtype : (gt == at::kFloat ? BEVK_DTYPE_F32 : p.dtype);
+  if (!first && gt != at::kFloat)
+    TORCH_CHECK(gt == offset.scalar_type(),
+                "bevk: dcn_backward_data: gradients must be float32 or the input dtype");
+  a.dcol_ld = dc.defined() ? dc.stride(0) : 0;
+  a.col_ld = cl.defined() ? cl.stride(0) : 0;
+  const c10::cuda::CUDAGuard guard(offset.device());
+  Tensor ws;
+  if (gi.defined()) {
+    const size_t bytes = bevk_dcn_backward_data_workspace_bytes(&p);
+    ws = at::empty({static_cast<int64_t>(bytes)}, offset.options().dtype(at::kByte));
+  }
+  auto ptr = [](const Tensor &t) { return t.defined() ? t.data_ptr() : nullptr; };
+  const int st = bevk_dcn_backward_data(&a, ptr(in), offset.data_ptr(), mask.data_ptr(), ptr(dc),
+                                        ptr(gi), ptr(go), ptr(gm), ptr(cl), ptr(ws),
+                                        ws.defined() ? static_cast<size_t>(ws.numel()) : 0,
+                                        current_stream(offset));
+  if (st == BEVK_ERR_UNSUPPORTED) return false;
+  check_status(st, "dcn_backward_data");
+  return true;
+}
+
 // Deformable columns of NCHW-shaped tensors in any memory format: layout 0
 // [C*kH*kW, M], layout 1 [M, kH*kW*C].
 Tensor dcn_columns(const Tensor &input, const Tensor &offset, const Tensor &mask,
@@ -509,6 +601,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("kernel_w"), py::arg("stride_h"), py::arg("stride_w"), py::arg("pad_h"),
         py::arg("pad_w"), py::arg("dil_h"), py::arg("dil_w"), py::arg("deform_groups"),
         py::arg("grad_input"), py::arg("grad_offset"), py::arg("grad_mask"));
+  m.def("dcn_backward_data", &dcn_backward_data,
+        "DCN backward data side without floating-point atomics: grad_input / grad_offset / "
+        "grad_mask (written) and the NHWC column matrix; False when the layout is not covered",
+        py::arg("dcol"), py::arg("input"), py::arg("offset"), py::arg("mask"),
+        py::arg("mask_is_logit"), py::arg("in_channels"), py::arg("height"), py::arg("width"),
+        py::arg("kernel_h"), py::arg("kernel_w"), py::arg("stride_h"), py::arg("stride_w"),
+        py::arg("pad_h"), py::arg("pad_w"), py::arg("dil_h"), py::arg("dil_w"),
+        py::arg("deform_groups"), py::arg("grad_input"), py::arg("grad_offset"),
+        py::arg("grad_mask"), py::arg("col"));
   m.def("dcn_columns", &dcn_columns,
         "Deformable column matrix (layout 0: [C*kH*kW, M], 1: [M, kH*kW*C])",
         py::arg("input"), py::arg("offset"), py::arg("mask"), py::arg("kernel_h"),

@@ -18,7 +18,8 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from .modulated_deform_conv import _load_ext, _tap_major_weight, dcn_forward_into, offset_conv
+from .modulated_deform_conv import (_load_ext, _ones_pad, _tap_major_weight, dcn_forward_into,
+                                    offset_conv)
 
 
 def out_size(H, pad, dil, k, stride):
@@ -164,23 +165,47 @@ class DCNSplitNHWCFunction(torch.autograd.Function):
         dO = go.to(dt)
         w_tap = _tap_major_weight(weight, dt)                             # [Cout, K], k = t*Cin + c
         dcol = torch.mm(dO, w_tap)                                        # [M, K]
-        y_nhwc = y.permute(0, 2, 3, 1).contiguous()                       # [B, Ho, Wo, 3T]
-        gX = torch.zeros(B, H, W, Cin, device=x.device, dtype=torch.float32)
-        gOff = torch.zeros(B, Ho, Wo, 2 * T, device=x.device, dtype=torch.float32)
-        gMask = torch.zeros(B, Ho, Wo, T, device=x.device, dtype=torch.float32)
-        ext.modulated_deformable_col2im_nhwc_cuda(
-            dcol, x.contiguous(), y_nhwc, y_nhwc, B, Cin, H, W, Ho, Wo, kH, kW, pd, pd, st, st,
-            dl, dl, 1, gX, gOff, gMask)
-        cols = gather_cols_nhwc(x, y_nhwc, None, kH, kW, st, pd, dl)      # [M, K]
+        xc = x.contiguous()
+        # fp32 gradients: gX meets the offset conv's input gradient, gOff /
+        # gMask (one [B, Ho, Wo, 3T] buffer, the offset conv's dY) feed its
+        # backward
+        gX = torch.empty(B, H, W, Cin, device=x.device, dtype=torch.float32)
+        dY_nhwc = torch.empty(B, Ho, Wo, 3 * T, device=x.device, dtype=torch.float32)
+        # with a bias, 8 more columns [1, 0, ..., 0]: the grad_weight GEMM then
+        # also returns the column sums of dO (grad_bias)
+        Kc = K + 8 if ctx.with_bias else K
+        cols = torch.empty(M, Kc, device=x.device, dtype=dt)
+        # offsets and pre-sigmoid mask read straight from the offset-conv output
+        done = ext.dcn_backward_data(
+            dcol, xc.permute(0, 3, 1, 2), y[:, :2 * T], y[:, 2 * T:], True, Cin, H, W, kH, kW,
+            st, st, pd, pd, dl, dl, 1, gX.permute(0, 3, 1, 2),
+            dY_nhwc[..., :2 * T].permute(0, 3, 1, 2), dY_nhwc[..., 2 * T:].permute(0, 3, 1, 2),
+            cols[:, :K])
+        if done:
+            gOff, gMask = dY_nhwc[..., :2 * T], dY_nhwc[..., 2 * T:]
+            if Kc > K:
+                cols[:, K:].copy_(_ones_pad(dt, x.device).expand(M, 8))
+        else:
+            y_nhwc = y.permute(0, 2, 3, 1).contiguous()                   # [B, Ho, Wo, 3T]
+            gX.zero_()
+            gOff = torch.zeros(B, Ho, Wo, 2 * T, device=x.device, dtype=torch.float32)
+            gMask = torch.zeros(B, Ho, Wo, T, device=x.device, dtype=torch.float32)
+            ext.modulated_deformable_col2im_nhwc_cuda(
+                dcol, xc, y_nhwc, y_nhwc, B, Cin, H, W, Ho, Wo, kH, kW, pd, pd, st, st,
+                dl, dl, 1, gX, gOff, gMask)
+            cols = gather_cols_nhwc(x, y_nhwc, None, kH, kW, st, pd, dl)  # [M, K]
         # fp16/bf16 operands, fp32 products and accumulation: the reference's
         # fp32 GEMM of the up-cast operands without the up-cast copies
         gw32 = (torch.mm(cols.t(), dO, out_dtype=torch.float32)
                 if dt in (torch.float16, torch.bfloat16) else torch.mm(cols.t().float(), dO.float()))
-        grad_weight = gw32 \
+        grad_bias = None
+        if ctx.with_bias:
+            grad_bias = (gw32[K] if cols.shape[1] > K else dO.sum(0, dtype=torch.float32)).to(dt)
+        grad_weight = gw32[:K] \
             .view(kH, kW, Cin, Cout).permute(3, 2, 0, 1).contiguous().to(dt)
-        grad_bias = dO.sum(0, dtype=torch.float32).to(dt) if ctx.with_bias else None
         # offset / mask convolution backward (regular convolution)
-        dY = torch.cat([gOff, gMask], dim=-1).permute(0, 3, 1, 2).contiguous()   # [B, 3T, Ho, Wo]
+        dY = (dY_nhwc if done else torch.cat([gOff, gMask], dim=-1)) \
+            .permute(0, 3, 1, 2).contiguous()                            # [B, 3T, Ho, Wo]
         x_nchw = x.permute(0, 3, 1, 2).float()
         w_off_f = w_off.float()
         grad_x_off = tnng.conv2d_input(x_nchw.shape, w_off_f, dY, st, pd, dl)

@@ -289,6 +289,21 @@ def _tap_major_weight(weight, dtype):
     return wt
 
 
+_ONES_PAD = {}
+
+
+def _ones_pad(dtype, device):
+    """[1, 0, 0, 0, 0, 0, 0, 0]: the extra columns that make the grad_weight
+    GEMM return grad_bias (cached per dtype and device)."""
+    key = (dtype, device)
+    t = _ONES_PAD.get(key)
+    if t is None:
+        t = torch.zeros(8, dtype=dtype, device=device)
+        t[0] = 1
+        _ONES_PAD[key] = t
+    return t
+
+
 def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dilation,
                  groups=1, deform_groups=1, need_input=True, need_offset_mask=True,
                  need_weight=True, need_bias=True):
@@ -298,10 +313,14 @@ def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dila
 
     The two contractions are plain GEMMs (cuBLAS through torch.mm, as in the
     reference): the column gradient dcol = dO . W^T in pixel-major NHWC order
-    [M, kH*kW*C] (k = t*C + c), and grad_weight = dO^T . col with col from the
-    deformable im2col kernel.  The deformable part -- scatter of dcol into
-    grad_input and the offset / mask gradients -- is the bevk_dcn_col2im
-    kernel, which accumulates in fp32 (fp64 for fp64).
+    [M, kH*kW*C] (k = t*C + c), and grad_weight = dO^T . col.  The deformable
+    part is bevk_dcn_backward_data for fp32/fp16/bf16 with channel counts in
+    whole 16-byte vectors (the input is read channels-last, copied once if it
+    is not): grad_input summed per destination pixel after a counting sort of
+    the samples' corners, grad_offset / grad_mask and col from one pass over
+    the samples, all written in the output dtype.  Other cases take the
+    bevk_dcn_col2im scatter (fp32 atomics; fp64 for fp64) and the im2col
+    kernel.
     """
     ext = _load_ext()
     B, C, H, W = input.shape
@@ -320,6 +339,7 @@ def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dila
     go = grad_output.to(dt).permute(0, 2, 3, 1).reshape(M, Cout)    # [M, Cout]
 
     grad_input = grad_offset = grad_mask = grad_weight = grad_bias = None
+    col = None
     if need_input or need_offset_mask:
         # dcol[m, t*C + c] = sum_co dO[m, co] * weight[co, c_local, t]  (per conv group)
         wt = _tap_major_weight(weight, dt).view(G, Coutg, T * Cg)          # k = t*Cg + c
@@ -329,26 +349,59 @@ def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dila
             dcol = torch.stack([torch.mm(go[:, g * Coutg:(g + 1) * Coutg], wt[g])
                                 for g in range(G)], 1)                      # [M, G, T*Cg]
             dcol = dcol.view(M, G, T, Cg).permute(0, 2, 1, 3).reshape(M, T * C)
-        fmt = (torch.channels_last if input.is_contiguous(memory_format=torch.channels_last)
-               else torch.contiguous_format)
-        gx = (torch.zeros(B, C, H, W, device=input.device, dtype=acc).contiguous(
-            memory_format=fmt) if need_input else None)
-        goff = torch.zeros(offset.shape, device=input.device, dtype=acc) if need_offset_mask else None
-        gmsk = torch.zeros(mask.shape, device=input.device, dtype=acc) if need_offset_mask else None
-        ext.dcn_col2im(dcol, input if need_offset_mask else None, offset, mask, C, H, W, kH, kW,
-                       sh, sw, ph, pw, dh, dw, deform_groups, gx, goff, gmsk)
-        if need_input:
-            grad_input = gx.to(dt)
-        if need_offset_mask:
-            grad_offset = goff.to(offset.dtype)
-            grad_mask = gmsk.to(mask.dtype)
+        done = False
+        if dt != torch.float64 and (C * input.element_size()) % 16 == 0:
+            dev = input.device
+            x_cl = None
+            if need_offset_mask or need_weight:
+                x_cl = input.contiguous(memory_format=torch.channels_last)
+            gx = (torch.empty(B, C, H, W, device=dev, dtype=dt).contiguous(
+                memory_format=torch.channels_last) if need_input else None)
+            goff = torch.empty(offset.shape, device=dev, dtype=dt) if need_offset_mask else None
+            gmsk = torch.empty(mask.shape, device=dev, dtype=dt) if need_offset_mask else None
+            # with a bias, 8 more columns [1, 0, ..., 0]: the grad_weight GEMM
+            # then also returns the column sums of dO (grad_bias)
+            K = T * C
+            ones_col = need_weight and need_bias and G == 1
+            col = (torch.empty(M, K + 8 if ones_col else K, device=dev, dtype=dt)
+                   if need_weight else None)
+            done = ext.dcn_backward_data(dcol, x_cl, offset, mask, False, C, H, W, kH, kW, sh, sw,
+                                         ph, pw, dh, dw, deform_groups, gx, goff, gmsk,
+                                         None if col is None else col[:, :K])
+            if done:
+                grad_input, grad_offset, grad_mask = gx, goff, gmsk
+                if ones_col:
+                    col[:, K:].copy_(_ones_pad(dt, dev).expand(M, 8))
+            else:
+                col = None
+        if not done:
+            fmt = (torch.channels_last if input.is_contiguous(memory_format=torch.channels_last)
+                   else torch.contiguous_format)
+            gx = (torch.zeros(B, C, H, W, device=input.device, dtype=acc).contiguous(
+                memory_format=fmt) if need_input else None)
+            goff = (torch.zeros(offset.shape, device=input.device, dtype=acc)
+                    if need_offset_mask else None)
+            gmsk = (torch.zeros(mask.shape, device=input.device, dtype=acc)
+                    if need_offset_mask else None)
+            ext.dcn_col2im(dcol, input if need_offset_mask else None, offset, mask, C, H, W, kH,
+                           kW, sh, sw, ph, pw, dh, dw, deform_groups, gx, goff, gmsk)
+            if need_input:
+                grad_input = gx.to(dt)
+            if need_offset_mask:
+                grad_offset = goff.to(offset.dtype)
+                grad_mask = gmsk.to(mask.dtype)
     if need_weight:
-        # NHWC column matrix [M, T*C] (k = t*C + c; aligned leading dimensions
-        # for the GEMM) gathered straight from the input in its own layout
-        col = ext.dcn_columns(input, offset, mask, kH, kW, sh, sw, ph, pw, dh, dw,
-                              deform_groups, 1)
+        if col is None:
+            # NHWC column matrix [M, T*C] (k = t*C + c; aligned leading
+            # dimensions for the GEMM) gathered straight from the input in its
+            # own layout
+            col = ext.dcn_columns(input, offset, mask, kH, kW, sh, sw, ph, pw, dh, dw,
+                                  deform_groups, 1)
         if G == 1:
-            gw = torch.mm(go.t(), col)                                   # [Cout, T*C]
+            gw = torch.mm(go.t(), col)                                   # [Cout, T*C (+8)]
+            if gw.shape[1] > T * C:
+                grad_bias = gw[:, T * C].contiguous()
+                gw = gw[:, :T * C]
             gw = gw.view(Cout, kH, kW, C).permute(0, 3, 1, 2)
         else:
             colg = col.view(M, T, G, Cg)
@@ -356,7 +409,7 @@ def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dila
                                      colg[:, :, g].reshape(M, T * Cg)) for g in range(G)], 0)
             gw = gw.view(Cout, kH, kW, Cg).permute(0, 3, 1, 2)
         grad_weight = gw.contiguous().to(weight.dtype)
-    if need_bias:
+    if need_bias and grad_bias is None:
         grad_bias = go.sum(0, dtype=acc).to(dt)
     return grad_input, grad_offset, grad_mask, grad_weight, grad_bias
 

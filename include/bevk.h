@@ -320,6 +320,62 @@ BEVK_API int bevk_dcn_col2im(const bevk_dcn_col2im_args *args, const void *input
                              bevk_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* DCNv2 backward: data side in one call, without floating-point atomics    */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Arguments of bevk_dcn_backward_data.  `problem` as for bevk_dcn_col2im
+ * (geometry, dtype f32 / f16 / bf16, input / offset / mask strides,
+ * mask_is_logit).  dcol and col are NHWC column matrices [M, kH*kW*C]
+ * (element (m, t*C + c) at m*ld + t*C + c, m = (b*Ho + oh)*Wo + ow) in the
+ * problem dtype with row strides dcol_ld / col_ld.  The three gradients are
+ * stored in grad_dtype (the problem dtype or BEVK_DTYPE_F32) with the given
+ * element strides (b, channel, h, w).
+ */
+typedef struct bevk_dcn_backward_data_args {
+  bevk_dcn_problem problem;
+  int grad_dtype;
+  int64_t dcol_ld;
+  int64_t col_ld;
+  int64_t grad_input_strides[4];
+  int64_t grad_offset_strides[4];
+  int64_t grad_mask_strides[4];
+} bevk_dcn_backward_data_args;
+
+/* Device workspace bytes bevk_dcn_backward_data needs when grad_input is
+ * requested (destination buckets of the samples' corners); 0 otherwise. */
+BEVK_API size_t bevk_dcn_backward_data_workspace_bytes(const bevk_dcn_problem *p);
+
+/*
+ * replaces the data side of the backward -- col2im_nhwc + col2im_coord_nhwc +
+ * im2col_nhwc (csrc/binding.cpp:63-140) as DCNSplitNHWCFunction.backward runs
+ * them (dcn_split_nhwc.py:231-291, col2im_nhwc :48-120) and the col2im /
+ * col2im_coord / im2col calls of ModulatedDeformConv2dFunction.backward
+ * (modulated_deform_conv.py:405-499) -- for channel-contiguous input, column
+ * and grad_input layouts.  WRITES (does not accumulate):
+ *   grad_input  [b, c, h, w] = sum of dcol * mask * (bilinear corner weight)
+ *                over the samples whose in-range corners include (h, w)
+ *                (0 where none lands)
+ *   grad_offset, grad_mask    the values bevk_dcn_col2im adds
+ *   col[m, t*C + c]           = mask * bilinear(input), the columns of the
+ *                grad_weight GEMM (bit-identical to bevk_dcn_columns layout 1)
+ * Any of grad_input / grad_offset / grad_mask / col may be NULL to skip it;
+ * input may be NULL when only grad_input is wanted, dcol when only col is.
+ * grad_input is summed in registers per destination after a counting sort of
+ * the samples' corners (the workspace), not by atomics; the summation order
+ * inside a destination follows the sort's integer atomics, so its last bits
+ * may vary between runs.  Layouts: input channel stride 1 (when read),
+ * grad_input channel stride 1, C / (C / deformable_groups) / the row strides
+ * whole 16-byte vectors, 16-byte-aligned pointers; otherwise
+ * BEVK_ERR_UNSUPPORTED (bevk_dcn_col2im + bevk_dcn_columns cover any layout).
+ */
+BEVK_API int bevk_dcn_backward_data(const bevk_dcn_backward_data_args *args,
+                                    const void *input, const void *offset, const void *mask,
+                                    const void *dcol, void *grad_input, void *grad_offset,
+                                    void *grad_mask, void *col, void *workspace,
+                                    size_t workspace_bytes, bevk_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Multi-scale deformable attention, forward                                */
 /* ------------------------------------------------------------------------ */
 
