@@ -14,22 +14,22 @@
 //
 // grad_input.  The reference scatters every (sample, corner, channel) product
 // into grad_input with floating-point atomics; on this part that runs at the
-// L2's atomic rate.  Here the samples are bucketed by destination pixel with a
-// counting sort and every grad_input element is summed in registers and
-// written once:
+// L2's atomic rate.  Here the samples' corners are bucketed by destination
+// pixel with a counting sort and every grad_input element is summed in
+// registers and written once:
 //   1. dcn_bwd_count_kernel  -- one thread per sample counts its in-range
 //      corners per destination bucket (b, deformable group, y, x) with integer
-//      atomics;
+//      reductions;
 //   2. dcn_bwd_scan_kernel   -- one CTA turns the counts into bucket ends
 //      (inclusive prefix sums, in place);
-//   3. dcn_bwd_sample_kernel -- one warp per sample: its lanes 0-3 take a slot
-//      in each in-range corner's bucket (decrementing the end, so the array
-//      holds the bucket starts afterwards) and store (dcol row offset, weight);
-//      all lanes compute the column row and the three per-sample channel sums
-//      of the coordinate gradients from the four corner lines;
+//   3. dcn_bwd_fill_kernel   -- one thread per sample takes a slot in each
+//      in-range corner's bucket (decrementing the end, so the array holds the
+//      bucket starts afterwards) and stores (dcol row offset, weight);
 //   4. dcn_bwd_gradx_kernel  -- one group of lanes per (bucket, channel chunk)
 //      sums its entries' dcol vectors times the weights in fp32 and writes the
-//      grad_input vector: no zeroing pass, no fp32 workspace, no cast pass.
+//      grad_input vector: no zeroing pass, no fp32 workspace, no cast pass;
+//   5. dcn_bwd_sample_kernel -- one warp per (pixel, 3 taps): the column rows
+//      and the coordinate gradients.
 // Count and fill derive a sample's corners from the same arithmetic on the
 // same offsets, so each bucket receives exactly the entries it counted.  The
 // order of the entries inside a bucket follows the order of the fill atomics,
@@ -83,12 +83,36 @@ __device__ __forceinline__ float2 pair_at(const uint4 &u, int i) {
   if constexpr (std::is_same_v<T, float>) {
     return make_float2(__uint_as_float(word(u, 2 * i)), __uint_as_float(word(u, 2 * i + 1)));
   } else if constexpr (std::is_same_v<T, __half>) {
-    const uint32_t w = word(u, i);
-    return make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu))),
-                       __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16))));
+    __half2 h;
+    *reinterpret_cast<uint32_t *>(&h) = word(u, i);
+    return __half22float2(h);
   } else {
     const uint32_t w = word(u, i);
     return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  }
+}
+
+// d0 += a.lo * b.lo, d1 += a.hi * b.hi for channel pair i of two 16-byte
+// vectors.  fp16 / bf16 operands go straight from their packed words into
+// mixed-precision FMAs (the product of two 16-bit floats is exact in fp32, so
+// each step rounds once, exactly as an fp32 FMA of the converted operands);
+// fp32 operands use fmaf.
+template <typename T>
+__device__ __forceinline__ void fma_pair(float &d0, float &d1, const uint4 &a, const uint4 &b,
+                                         int i) {
+  if constexpr (std::is_same_v<T, float>) {
+    d0 = fmaf(__uint_as_float(word(a, 2 * i)), __uint_as_float(word(b, 2 * i)), d0);
+    d1 = fmaf(__uint_as_float(word(a, 2 * i + 1)), __uint_as_float(word(b, 2 * i + 1)), d1);
+  } else if constexpr (std::is_same_v<T, __half>) {
+    asm("{\n\t.reg .b16 a0, a1, b0, b1;\n\tmov.b32 {a0, a1}, %2;\n\tmov.b32 {b0, b1}, %3;\n\t"
+        "fma.rn.f32.f16 %0, a0, b0, %0;\n\tfma.rn.f32.f16 %1, a1, b1, %1;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "r"(word(a, i)), "r"(word(b, i)));
+  } else {
+    asm("{\n\t.reg .b16 a0, a1, b0, b1;\n\tmov.b32 {a0, a1}, %2;\n\tmov.b32 {b0, b1}, %3;\n\t"
+        "fma.rn.f32.bf16 %0, a0, b0, %0;\n\tfma.rn.f32.bf16 %1, a1, b1, %1;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "r"(word(a, i)), "r"(word(b, i)));
   }
 }
 
@@ -281,7 +305,7 @@ dcn_bwd_fill_kernel(const BwdDataParams p, const T *__restrict__ off, const T *_
   }
 }
 
-constexpr int kSampleWarps = 4;
+constexpr int kSampleWarps = 1;  // one-warp CTAs: measured fastest (more CTAs in flight)
 constexpr int kOutside = -(1 << 20);  // h_low of a sample outside the gate: no corner in range
 
 // One warp per (output pixel, deformable group, group of `tpw` taps).  Lane j
@@ -372,6 +396,7 @@ dcn_bwd_sample_kernel(const BwdDataParams p, const T *__restrict__ x, const T *_
     float2 D[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) D[k] = make_float2(0.f, 0.f);
+#pragma unroll 2
     for (int c = lane * V; c < p.cpg; c += 32 * V) {
       uint4 xr[4];
 #pragma unroll
@@ -384,17 +409,17 @@ dcn_bwd_sample_kernel(const BwdDataParams p, const T *__restrict__ x, const T *_
 #pragma unroll
       for (int i = 0; i < V / 2; ++i) {
         // column value: corners in order, products with the mask-folded
-        // weights (the im2col kernel's arithmetic, two channels at a time)
-        const float2 d2 = pair_at<T>(dr, i);
-        float2 a2 = make_float2(0.f, 0.f);
+        // weights (the im2col kernel's arithmetic)
+        float a0 = 0.f, a1 = 0.f;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const float2 x2 = pair_at<T>(xr[k], i);
-          a2 = __ffma2_rn(make_float2(wm[k], wm[k]), x2, a2);
-          D[k] = __ffma2_rn(d2, x2, D[k]);
+          a0 = fmaf(wm[k], x2.x, a0);
+          a1 = fmaf(wm[k], x2.y, a1);
+          fma_pair<T>(D[k].x, D[k].y, dr, xr[k], i);
         }
-        cv[2 * i] = a2.x;
-        cv[2 * i + 1] = a2.y;
+        cv[2 * i] = a0;
+        cv[2 * i + 1] = a1;
       }
       if (col_row != nullptr) st_vec<T, V>(col_row + c, cv);
     }
@@ -535,47 +560,47 @@ int launch_typed(const BwdDataParams &p, const void *input, const void *offset,
     st = check_launch("dcn_bwd_scan_kernel");
     if (st != BEVK_OK) return st;
   }
-  const bool need_x = grad_offset != nullptr || grad_mask != nullptr || col != nullptr;
   if (grad_input != nullptr) {
-    const int64_t blocks = std::min<int64_t>((p.units + 255) / 256, max_blocks);
-    dcn_bwd_fill_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+    const int64_t fblocks = std::min<int64_t>((p.units + 255) / 256, max_blocks);
+    dcn_bwd_fill_kernel<T><<<static_cast<unsigned>(fblocks), 256, 0, stream>>>(
         p, off, static_cast<const T *>(mask), cnt, entries);
-    const int st = check_launch("dcn_bwd_fill_kernel");
+    int st = check_launch("dcn_bwd_fill_kernel");
+    if (st != BEVK_OK) return st;
+    // The gather runs before the sample kernel, while the column gradient
+    // (written just before this call) is still in L2.  Lanes per bucket:
+    // enough for the group's channel vectors (a power of two, at most 32);
+    // two vectors per lane once a warp's 32 lanes would otherwise take a
+    // bucket in two or more chunks.
+    const int nvec = (p.cpg + V - 1) / V;
+    int lpg_log2 = 0;
+    while ((1 << lpg_log2) < nvec && lpg_log2 < 5) ++lpg_log2;
+    const int lpg = 1 << lpg_log2;
+    const int vpl = nvec >= 2 * lpg ? 2 : 1;
+    const int nchunks = (nvec + vpl * lpg - 1) / (vpl * lpg);
+    const int64_t threads = static_cast<int64_t>(p.nb) * nchunks * lpg;
+    const int64_t gblocks = (threads + kGatherThreads - 1) / kGatherThreads;
+    if (gblocks > 0x7FFFFFFF)
+      return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn backward data: grid too large");
+    auto kern = vpl == 2 ? dcn_bwd_gradx_kernel<T, TG, 2> : dcn_bwd_gradx_kernel<T, TG, 1>;
+    kern<<<static_cast<unsigned>(gblocks), kGatherThreads, 0, stream>>>(
+        p, static_cast<const T *>(dcol), cnt, entries, static_cast<TG *>(grad_input), lpg_log2,
+        nchunks);
+    st = check_launch("dcn_bwd_gradx_kernel");
     if (st != BEVK_OK) return st;
   }
-  if (need_x) {
-    // taps per warp: threes for the usual 3-wide kernels, else all taps (at
-    // most 32)
-    const int tpw = p.T % 3 == 0 ? 3 : std::min(p.T, 32);
-    const int ngroups = (p.T + tpw - 1) / tpw;
-    const int64_t warps = p.M * p.dg * ngroups;
-    if (warps > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn backward data: grid too large");
-    const int64_t blocks = (warps + kSampleWarps - 1) / kSampleWarps;
-    dcn_bwd_sample_kernel<T, TG><<<static_cast<unsigned>(blocks), kSampleWarps * 32, 0, stream>>>(
-        p, static_cast<const T *>(input), off, static_cast<const T *>(mask),
-        static_cast<const T *>(dcol), static_cast<TG *>(grad_offset),
-        static_cast<TG *>(grad_mask), static_cast<T *>(col), tpw, ngroups);
-    const int st = check_launch("dcn_bwd_sample_kernel");
-    if (st != BEVK_OK) return st;
-  }
-  if (grad_input == nullptr) return BEVK_OK;
-  // lanes per bucket: enough for the group's channel vectors (a power of
-  // two, at most 32); two vectors per lane once a warp's 32 lanes would
-  // otherwise take a bucket in two or more chunks
-  const int nvec = (p.cpg + V - 1) / V;
-  int lpg_log2 = 0;
-  while ((1 << lpg_log2) < nvec && lpg_log2 < 5) ++lpg_log2;
-  const int lpg = 1 << lpg_log2;
-  const int vpl = nvec >= 2 * lpg ? 2 : 1;
-  const int nchunks = (nvec + vpl * lpg - 1) / (vpl * lpg);
-  const int64_t threads = static_cast<int64_t>(p.nb) * nchunks * lpg;
-  const int64_t blocks = (threads + kGatherThreads - 1) / kGatherThreads;
-  if (blocks > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn backward data: grid too large");
-  auto kern = vpl == 2 ? dcn_bwd_gradx_kernel<T, TG, 2> : dcn_bwd_gradx_kernel<T, TG, 1>;
-  kern<<<static_cast<unsigned>(blocks), kGatherThreads, 0, stream>>>(
-      p, static_cast<const T *>(dcol), cnt, entries, static_cast<TG *>(grad_input), lpg_log2,
-      nchunks);
-  return check_launch("dcn_bwd_gradx_kernel");
+  if (grad_offset == nullptr && grad_mask == nullptr && col == nullptr) return BEVK_OK;
+  // taps per warp: threes for the usual 3-wide kernels, else all taps (at
+  // most 32)
+  const int tpw = p.T % 3 == 0 ? 3 : std::min(p.T, 32);
+  const int ngroups = (p.T + tpw - 1) / tpw;
+  const int64_t warps = p.M * p.dg * ngroups;
+  if (warps > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn backward data: grid too large");
+  const int64_t blocks = (warps + kSampleWarps - 1) / kSampleWarps;
+  dcn_bwd_sample_kernel<T, TG><<<static_cast<unsigned>(blocks), kSampleWarps * 32, 0, stream>>>(
+      p, static_cast<const T *>(input), off, static_cast<const T *>(mask),
+      static_cast<const T *>(dcol), static_cast<TG *>(grad_offset),
+      static_cast<TG *>(grad_mask), static_cast<T *>(col), tpw, ngroups);
+  return check_launch("dcn_bwd_sample_kernel");
 }
 
 }  // namespace
