@@ -361,10 +361,12 @@ def bench_dcn_pack(cfg_name, steps, warmup, device, seed, stream, fused):
 
 
 def bench_dcn_bwd(cfg_name, steps, warmup, device, seed, stream):
-    """DCN backward as autograd runs it: dO . W^T (GEMM), the col2im scatter
-    into grad_input / grad_offset / grad_mask, the im2col gather and
-    dO^T . col (GEMM) for grad_weight, and grad_bias.  FLOPs counted: the two
-    GEMMs (2 x the forward's 2*M*N*K)."""
+    """DCN backward as autograd runs it: dO . W^T (GEMM), the data side
+    (bevk_dcn_backward_data: grad_input by a counting sort of the sample
+    corners and a gather, grad_offset / grad_mask and the grad_weight columns
+    from one pass over the samples) and [dO^T . col | ones] (GEMM) for
+    grad_weight and grad_bias.  FLOPs counted: the two GEMMs (2 x the
+    forward's 2*M*N*K)."""
     import torch
     import modulated_deform_conv as mdc
     cfg = DCN_CFGS[cfg_name]
