@@ -398,11 +398,13 @@ def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dila
             col = ext.dcn_columns(input, offset, mask, kH, kW, sh, sw, ph, pw, dh, dw,
                                   deform_groups, 1)
         if G == 1:
-            gw = torch.mm(go.t(), col)                                   # [Cout, T*C (+8)]
-            if gw.shape[1] > T * C:
-                grad_bias = gw[:, T * C].contiguous()
-                gw = gw[:, :T * C]
-            gw = gw.view(Cout, kH, kW, C).permute(0, 3, 1, 2)
+            # col^T . dO ([T*C (+8), Cout]) is the faster cuBLAS form of this
+            # product on B200 than dO^T . col (36 vs 42 us at the stage-4 shape)
+            gwt = torch.mm(col.t(), go)                                  # [T*C (+8), Cout]
+            if gwt.shape[0] > T * C:
+                grad_bias = gwt[T * C].contiguous()
+                gwt = gwt[:T * C]
+            gw = gwt.view(kH, kW, C, Cout).permute(3, 2, 0, 1)
         else:
             colg = col.view(M, T, G, Cg)
             gw = torch.cat([torch.mm(go[:, g * Coutg:(g + 1) * Coutg].t(),
