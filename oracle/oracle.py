@@ -15,9 +15,11 @@ Parity status:
     stand-ins in ``oracle/ref_shim`` (``reference_msda_forward``; built into
     ``oracle/_ref`` by ``make -C oracle ref``), and cross-checked against the
     independent grid_sample formulation in ``oracle/msda_grid_sample.py``.
-  * MSDA backward: restated from :425-494 and :638-788 and pinned only through
-    torch autograd of the grid_sample formulation (the reference's backward
-    kernels are warp- and block-cooperative and do not run single-threaded).
+  * MSDA backward: restated from :425-494 and :638-788 and pinned against the
+    reference's own generic backward kernel (:1168-1271, block-cooperative)
+    run on the host as one emulated block of C threads
+    (``reference_msda_backward``, same ``oracle/_ref`` build), and checked
+    against torch autograd of the grid_sample formulation.
 
 All functions take and return numpy arrays (float32 compute; inputs of other
 float dtypes are up-cast, which is how fp16/bf16 kernel outputs are checked).
@@ -221,6 +223,32 @@ def reference_msda_forward(value, spatial_shapes, level_start_index, sampling_lo
     if rc != 0:
         raise ValueError("ref_msda_forward_f32: problem too large")
     return out
+
+
+def reference_msda_backward(value, spatial_shapes, level_start_index, sampling_loc,
+                            attn_weight, grad_output):
+    """The reference's generic MSDA backward kernel
+    (csrc_musa/msda/ms_deform_attn_kernels.cuh:1168-1271 with :426-491, one
+    block of C threads per (batch, query, head) as binding_musa.mu:266-282
+    launches it) run on the host as one emulated block of C threads ->
+    (grad_value, grad_loc, grad_attn) float32, grad_value from zero; the pin
+    for msda_backward."""
+    lib = ctypes.CDLL(_REF_PATH)
+    value, loc, attn = _f32(value), _f32(sampling_loc), _f32(attn_weight)
+    g = _f32(grad_output)
+    shapes = np.ascontiguousarray(np.asarray(spatial_shapes, dtype=np.int64))
+    lsi = np.ascontiguousarray(np.asarray(level_start_index, dtype=np.int64))
+    B, S, M, C = value.shape
+    _, Q, _, L, P, _ = loc.shape
+    gv = np.zeros(value.shape, np.float32)
+    gl = np.zeros(loc.shape, np.float32)
+    ga = np.zeros(attn.shape, np.float32)
+    rc = lib.ref_msda_backward_f32(_p(value), shapes.ctypes.data_as(_i64p),
+                                   lsi.ctypes.data_as(_i64p), _p(loc), _p(attn), _p(g), B, S, M,
+                                   C, L, Q, P, _p(gv), _p(gl), _p(ga))
+    if rc != 0:
+        raise ValueError("ref_msda_backward_f32: problem too large or channels > 1024")
+    return gv, gl, ga
 
 
 def msda_backward(value, spatial_shapes, level_start_index, sampling_loc, attn_weight,

@@ -143,6 +143,44 @@ def test_msda_matches_reference_kernel(case):
     assert oracle.rel_l2(got, want) <= 1e-6 and oracle.max_abs(got, want) <= 1e-5
 
 
+REF_MSDA_BWD_CASES = [
+    # B, level shapes, heads, C, Q, P, spread of locations beyond [0, 1]
+    (2, [(20, 30)], 8, 32, 24, 4, 0.1),
+    (1, [(23, 41), (12, 21), (6, 11), (3, 6)], 8, 32, 12, 8, 0.1),
+    (1, [(9, 7), (5, 4)], 4, 32, 16, 13, 0.2),
+    (2, [(10, 12), (5, 6)], 3, 24, 10, 3, 0.1),      # C = 24: a block of 24 threads
+    (1, [(1, 1), (2, 1)], 8, 32, 8, 2, 0.3),         # degenerate levels
+]
+
+
+@pytest.mark.parametrize("case", REF_MSDA_BWD_CASES,
+                         ids=[f"b{i}" for i in range(len(REF_MSDA_BWD_CASES))])
+def test_msda_backward_matches_reference_kernel(case):
+    """The oracle's MSDA backward against the reference's own generic backward
+    kernel (ms_deform_attn_kernels.cuh:1168-1271: a block of C threads per
+    (batch, query, head), shared-memory reduction of the location / attention
+    gradients, atomics into grad_value) compiled for the host from the
+    reference tree and run as one emulated block of C host threads."""
+    if not oracle.reference_msda_available():
+        pytest.skip("reference tree not present and oracle/_ref not built")
+    B, shapes, M, C, Q, P, spread = case
+    rng = np.random.default_rng(len(shapes) * 1000 + Q + C)
+    L = len(shapes)
+    sizes = [h * w for h, w in shapes]
+    lsi = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.int64)
+    value = rng.standard_normal((B, sum(sizes), M, C)).astype(np.float32)
+    loc = rng.uniform(-spread, 1 + spread, (B, Q, M, L, P, 2)).astype(np.float32)
+    attn = rng.random((B, Q, M, L, P)).astype(np.float32)
+    gout = rng.standard_normal((B, Q, M * C)).astype(np.float32)
+    want = oracle.reference_msda_backward(value, np.array(shapes), lsi, loc, attn, gout)
+    got = oracle.msda_backward(value, np.array(shapes), lsi, loc, attn, gout)
+    # fp32 rounding only (summation orders and atomics differ)
+    for name, g, w in zip(("grad_value", "grad_loc", "grad_attn"), got, want):
+        scale = max(1.0, float(np.abs(w).max()))
+        assert oracle.rel_l2(g, w) <= 1e-5, (name, oracle.rel_l2(g, w))
+        assert oracle.max_abs(g, w) <= 1e-4 * scale, (name, oracle.max_abs(g, w))
+
+
 def test_msda_boundary_coordinates():
     """Points exactly on the gates: h = -1 and h = H (dropped), h = H-1 (kept)."""
     H, W = 4, 5
