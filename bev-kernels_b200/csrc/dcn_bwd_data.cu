@@ -92,6 +92,15 @@ __device__ __forceinline__ float2 pair_at(const uint4 &u, int i) {
   }
 }
 
+__device__ __forceinline__ __half2 u32_as_half2(uint32_t w) {
+  __half2 h;
+  *reinterpret_cast<uint32_t *>(&h) = w;
+  return h;
+}
+__device__ __forceinline__ uint32_t half2_as_u32(__half2 h) {
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
 // d0 += a.lo * b.lo, d1 += a.hi * b.hi for channel pair i of two 16-byte
 // vectors.  fp16 / bf16 operands go straight from their packed words into
 // mixed-precision FMAs (the product of two 16-bit floats is exact in fp32, so
@@ -390,6 +399,9 @@ dcn_bwd_sample_kernel(const BwdDataParams p, const T *__restrict__ x, const T *_
       xo[k] = valid[k] ? y * p.xs2 + xx * p.xs3 : 0;
       wm[k] = wk[k] * m0;  // the forward's corner weight, mask folded in
     }
+    __half2 w2[4];  // fp16 path: the weights as packed halves
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w2[k] = __float2half2_rn(wm[k]);
     const bool load_d = coord && h0 != kOutside;
     const T *dc_row = dcol + row_d + static_cast<int64_t>(t0 + j) * p.C;
     T *col_row = col != nullptr ? col + row_c + static_cast<int64_t>(t0 + j) * p.C : nullptr;
@@ -405,23 +417,43 @@ dcn_bwd_sample_kernel(const BwdDataParams p, const T *__restrict__ x, const T *_
                          : make_uint4(0, 0, 0, 0);
       const uint4 dr = load_d ? __ldg(reinterpret_cast<const uint4 *>(dc_row + c))
                               : make_uint4(0, 0, 0, 0);
-      float cv[V];
+      if constexpr (std::is_same_v<T, __half>) {
+        // fp16: the column values as the fused forward kernel builds its A
+        // tiles -- fp16 corner weights (mask folded in), a packed half2
+        // multiply and three FMAs per channel pair -- so no operand is
+        // converted to fp32 in this loop (the corner sums take the packed
+        // words directly)
+        uint32_t cw[4];
 #pragma unroll
-      for (int i = 0; i < V / 2; ++i) {
-        // column value: corners in order, products with the mask-folded
-        // weights (the im2col kernel's arithmetic)
-        float a0 = 0.f, a1 = 0.f;
+        for (int i = 0; i < 4; ++i) {
+          __half2 r = __hmul2(w2[0], u32_as_half2(word(xr[0], i)));
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 x2 = pair_at<T>(xr[k], i);
-          a0 = fmaf(wm[k], x2.x, a0);
-          a1 = fmaf(wm[k], x2.y, a1);
-          fma_pair<T>(D[k].x, D[k].y, dr, xr[k], i);
+          for (int k = 1; k < 4; ++k) r = __hfma2(w2[k], u32_as_half2(word(xr[k], i)), r);
+          cw[i] = half2_as_u32(r);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) fma_pair<T>(D[k].x, D[k].y, dr, xr[k], i);
         }
-        cv[2 * i] = a0;
-        cv[2 * i + 1] = a1;
+        if (col_row != nullptr)
+          *reinterpret_cast<uint4 *>(col_row + c) = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+      } else {
+        float cv[V];
+#pragma unroll
+        for (int i = 0; i < V / 2; ++i) {
+          // column value: corners in order, products with the mask-folded
+          // weights in fp32, rounded once (the im2col kernel's arithmetic)
+          float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 x2 = pair_at<T>(xr[k], i);
+            a0 = fmaf(wm[k], x2.x, a0);
+            a1 = fmaf(wm[k], x2.y, a1);
+            fma_pair<T>(D[k].x, D[k].y, dr, xr[k], i);
+          }
+          cv[2 * i] = a0;
+          cv[2 * i + 1] = a1;
+        }
+        if (col_row != nullptr) st_vec<T, V>(col_row + c, cv);
       }
-      if (col_row != nullptr) st_vec<T, V>(col_row + c, cv);
     }
     if (coord) {
       float d[4];

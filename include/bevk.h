@@ -358,7 +358,9 @@ BEVK_API size_t bevk_dcn_backward_data_workspace_bytes(const bevk_dcn_problem *p
  *                (0 where none lands)
  *   grad_offset, grad_mask    the values bevk_dcn_col2im adds
  *   col[m, t*C + c]           = mask * bilinear(input), the columns of the
- *                grad_weight GEMM (bit-identical to bevk_dcn_columns layout 1)
+ *                grad_weight GEMM (f32 / bf16: bit-identical to bevk_dcn_columns
+ *                layout 1; f16: built as bevk_dcn_forward builds its tiles,
+ *                fp16 corner weights and packed half2 FMAs)
  * Any of grad_input / grad_offset / grad_mask / col may be NULL to skip it;
  * input may be NULL when only grad_input is wanted, dcol when only col is.
  * grad_input is summed in registers per destination after a counting sort of

@@ -4,7 +4,9 @@ CPU oracle's DCN backward, and its column matrix against bevk_dcn_columns.
 
 Tolerances: fp32 within 1e-5 relative L2; fp16/bf16 within 5e-3 relative L2 of
 the fp32 oracle on the up-cast inputs; the column matrix bit-identical to the
-im2col kernel's.
+im2col kernel's for fp32 and bf16 (fp32 interpolation, rounded once), within
+2e-3 relative L2 of it for fp16 (built as the fused forward builds its
+tiles: fp16 weights, packed half2 FMAs).
 """
 import ctypes
 
@@ -74,7 +76,10 @@ def test_matches_oracle(cuda, case, dt):
         assert g.dtype == dt
         assert not torch.isnan(g).any(), name          # every element written
         assert rel_l2(g, torch.from_numpy(ref)) <= tol, (name, rel_l2(g, torch.from_numpy(ref)))
-    assert torch.equal(col, ref_col)
+    if dt == torch.float16:
+        assert rel_l2(col, ref_col) <= 2e-3, rel_l2(col, ref_col)
+    else:
+        assert torch.equal(col, ref_col)
 
 
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
