@@ -488,16 +488,19 @@ dcn_bwd_sample_kernel(const BwdDataParams p, const T *__restrict__ x, const T *_
   }
 }
 
-constexpr int kGatherThreads = 128, kGatherUnroll = 4;
+constexpr int kGatherThreads = 128;
 
 // One group of 2^lpg_log2 lanes per (bucket, chunk of VPL * 2^lpg_log2 * V
 // channels): each lane sums VPL channel vectors of its bucket's entries.
 template <typename T, typename TG, int VPL>
-__global__ void __launch_bounds__(kGatherThreads)
+__global__ void __launch_bounds__(kGatherThreads, 8)
 dcn_bwd_gradx_kernel(const BwdDataParams p, const T *__restrict__ dcol,
                      const int *__restrict__ starts, const uint2 *__restrict__ entries,
                      TG *__restrict__ gx, int lpg_log2, int nchunks) {
   constexpr int V = 16 / sizeof(T);
+  // entries per batch: loads in flight per lane = kUnroll * VPL, with the
+  // register budget of eight CTAs per SM
+  constexpr int kGatherUnroll = VPL == 2 ? 2 : 4;
   const int lane = threadIdx.x & 31;
   const int lpg = 1 << lpg_log2;
   const int li = lane & (lpg - 1);
