@@ -22,7 +22,11 @@ Also reported on the same line: ``e2e`` (the same metric through the public
 ``modulated_deform_conv2d`` call with inputs copied from pinned host memory and
 the output copied back every step), the roofline of the fused kernel against
 MEASURED_PEAKS.json, the CPU oracle timed on a bounded sample (rank 0, N = 1)
-and, in ``secondary``, BASELINE configs 3 (DCN bf16), 4 and 5 (MSDA fp32).
+and, in ``secondary``, BASELINE configs 3 (DCN bf16), 4 and 5 (MSDA fp32), the
+Pack forward, the DCN and MSDA backward, and the 5-chain (48 images, each a
+cfg5 MSDA camera slice and a cfg3 DCN image, in contiguous blocks per rank:
+strong scaling over the ranks, per-image checksums all-gathered and checked
+on rank 0 outside the timed region).
 
 ``--impl reference`` times the reference algorithm on the host cores instead
 (the CPU oracle restatement in oracle/, all threads) on the same workload and
@@ -232,6 +236,121 @@ def msda_sets(cfg, n_sets, seed, device):
                          shapes=torch.tensor(shapes, dtype=torch.int64, device=device),
                          lsi=torch.tensor(lsi, dtype=torch.int64, device=device)))
     return sets
+
+
+CHAIN_IMAGES = 48
+CHAIN_DESC = ("5-chain: 48 images (8 samples x 6 cameras); per image one cfg5 MSDA camera "
+              "slice (4 levels, Q=10000, 8x32, P=8, fp32) and one cfg3 DCN image (256 -> 256 "
+              "ch, 58x100, bf16, 5% offsets at +-(H+4)); contiguous image blocks per rank")
+
+
+def chain_inputs(img0, n, seed, device):
+    """Inputs of global images [img0, img0 + n) of the 5-chain: per image a cfg5
+    MSDA camera slice and a cfg3 DCN image, each generated from (seed, image
+    index) alone, so a rank's block holds exactly the same images as the
+    world-1 run (the DCN weight is shared, from the seed)."""
+    import torch
+    from bevk.sharding import image_seed
+    m5 = MSDA_CFGS["cfg5"]
+    M, C, Q, P = m5["M"], m5["C"], m5["Q"], m5["P"]
+    shapes = m5["shapes"]
+    L = len(shapes)
+    sizes = [h * w for h, w in shapes]
+    lsi = [0]
+    for sz in sizes[:-1]:
+        lsi.append(lsi[-1] + sz)
+    values, locs, attns = [], [], []
+    for img in range(img0, img0 + n):
+        g = torch.Generator(device=device)
+        g.manual_seed(image_seed(seed, img, 5))
+        values.append(torch.randn(1, sum(sizes), M, C, generator=g, device=device))
+        locs.append(torch.rand(1, Q, M, L, P, 2, generator=g, device=device))
+        attns.append(torch.softmax(torch.randn(1, Q, M, L * P, generator=g, device=device), -1)
+                     .view(1, Q, M, L, P))
+    msda = dict(value=torch.cat(values), loc=torch.cat(locs), attn=torch.cat(attns),
+                shapes=torch.tensor(shapes, dtype=torch.int64, device=device),
+                lsi=torch.tensor(lsi, dtype=torch.int64, device=device))
+    dcn = dcn_sets(dict(DCN_CFGS["cfg3"], B=n), 1, seed, img0, device)[0]
+    return msda, dcn
+
+
+def chain_step(msda, dcn):
+    """One 5-chain step over a block of images: the MSDA call and the DCN call."""
+    import _ms_deform_attn_ext as ext
+    import modulated_deform_conv as mdc
+    out = ext.forward(msda["value"], msda["shapes"], msda["lsi"], msda["loc"], msda["attn"], 64,
+                      False)
+    mdc.dcn_forward_into(dcn["x"], dcn["off"], dcn["mask"], dcn["w"], None, dcn["out"], 1, 1, 1)
+    return out, dcn["out"]
+
+
+def chain_checksums(msda_out, dcn_out):
+    """Per-image fp64 sums of both outputs -> [images, 2]."""
+    import torch
+    n = msda_out.shape[0]
+    if n == 0:
+        return torch.zeros(0, 2, dtype=torch.float64, device=msda_out.device)
+    return torch.stack([msda_out.double().reshape(n, -1).sum(1),
+                        dcn_out.double().reshape(n, -1).sum(1)], 1)
+
+
+def gather_rows(local, total, rank, world, dist):
+    """Rows [b0, b1) of a [total, k] table held by each rank (its shard_range
+    block) -> the whole table on every rank (an all_gather of equal-size,
+    padded blocks; NCCL or gloo)."""
+    import torch
+    from bevk.sharding import shard_range
+    if dist is None:
+        return local
+    width = max(shard_range(total, r, world)[1] - shard_range(total, r, world)[0]
+                for r in range(world))
+    pad = torch.full((width, local.shape[1]), float("nan"), dtype=local.dtype,
+                     device=local.device)
+    pad[:local.shape[0]] = local
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad)
+    rows = []
+    for r in range(world):
+        b0, b1 = shard_range(total, r, world)
+        rows.append(parts[r][:b1 - b0])
+    return torch.cat(rows)
+
+
+def bench_chain(steps, warmup, device, seed, stream, rank, world, dist):
+    """The 5-chain over the ranks: this rank's contiguous block of the 48 images
+    (no collective on the data path), K steps captured in graphs and timed
+    between events, max over ranks.  Outside the timed region, per-image output
+    checksums are all-gathered and rank 0 regenerates and recomputes every
+    rank's block (same block sizes, so the same kernels) and compares them."""
+    import torch
+    from bevk.sharding import shard_range
+    b0, b1 = shard_range(CHAIN_IMAGES, rank, world)
+    msda, dcn = chain_inputs(b0, b1 - b0, seed, device)
+    torch.cuda.synchronize()            # generated on the default stream, used on `stream`
+    ms = graph_time([lambda: chain_step(msda, dcn)], steps, warmup, stream, dist=dist)
+    with torch.cuda.stream(stream):
+        mine = chain_checksums(*chain_step(msda, dcn))
+    torch.cuda.synchronize()
+    del msda, dcn
+    table = gather_rows(mine, CHAIN_IMAGES, rank, world, dist)
+    verified = None
+    if rank == 0:
+        ok = bool(torch.isfinite(table).all())
+        for r in range(world):
+            r0, r1 = shard_range(CHAIN_IMAGES, r, world)
+            if r1 == r0:
+                continue
+            m, d = chain_inputs(r0, r1 - r0, seed, device)
+            torch.cuda.synchronize()
+            with torch.cuda.stream(stream):
+                again = chain_checksums(*chain_step(m, d))
+            torch.cuda.synchronize()
+            ok = ok and torch.equal(again.cpu(), table[r0:r1].cpu())
+            del m, d
+        verified = ok
+        torch.cuda.empty_cache()
+    return dict(ms=ms, per_step_s=ms / 1e3 / steps, images_per_rank=b1 - b0,
+                verified=verified)
 
 
 def n_sets_for(set_bytes, lo=2, hi=16):
@@ -584,7 +703,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--only", choices=("cfg2", "cfg3", "cfg4", "cfg5", "bwd_cfg2", "bwd_cfg3",
-                                       "bwd_cfg4", "bwd_cfg5", "pack_cfg2", "pack_cfg3"),
+                                       "bwd_cfg4", "bwd_cfg5", "pack_cfg2", "pack_cfg3",
+                                       "chain"),
                     help="time one workload's kernel only (profiling runs: no e2e, "
                          "secondary or CPU legs; prints a reduced line)")
     args = ap.parse_args()
@@ -614,7 +734,12 @@ def main():
     seed = 2026
 
     if args.only:
-        if args.only in DCN_CFGS:
+        if args.only == "chain":
+            r = bench_chain(args.steps, args.warmup, device, seed, stream, rank, world, dist)
+            r["per_launch_s"] = r["per_step_s"]
+            extra = {"images_per_s": CHAIN_IMAGES / r["per_step_s"], "verified": r["verified"],
+                     "n_gpus": world}
+        elif args.only in DCN_CFGS:
             r = bench_dcn(args.only, args.steps, args.warmup, device, seed, 0, stream, dist)
             del r["sets"]
             extra = {"tflops": r["flops"] / r["per_launch_s"] / 1e12}
@@ -717,6 +842,16 @@ def main():
                 "roofline_us": r["bytes"] / (peaks["hbm_gbs"] * 1e9) * 1e6,
                 "traffic": _traffic(f"msda_bwd {name}")}
             torch.cuda.empty_cache()
+        rc = bench_chain(min(k2, 20), args.warmup, device, seed + 6, stream, rank, world, dist)
+        secondary["chain_5"] = {
+            "workload": CHAIN_DESC, "images": CHAIN_IMAGES, "n_gpus": world,
+            "images_per_rank": rc["images_per_rank"], "ms_per_step": rc["per_step_s"] * 1e3,
+            "images_per_s": CHAIN_IMAGES / rc["per_step_s"], "scaling": "strong",
+            "verified": rc["verified"],
+            "verification": "per-image output checksums all-gathered to rank 0 outside the "
+                            "timed region and compared with rank 0's recomputation of every "
+                            "rank's block"}
+        torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -60,6 +60,33 @@ def _worker(rank, world, port):
         dist.destroy_process_group()
 
 
+def _gather_worker(rank, world, port, total):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        import bench
+        from bevk.sharding import shard_range
+        b0, b1 = shard_range(total, rank, world)
+        # rank r holds rows [b0, b1) of a table whose row i is (i, 10 i)
+        mine = torch.tensor([[float(i), 10.0 * i] for i in range(b0, b1)],
+                            dtype=torch.float64).reshape(-1, 2)
+        table = bench.gather_rows(mine, total, rank, world, dist)
+        want = torch.tensor([[float(i), 10.0 * i] for i in range(total)], dtype=torch.float64)
+        assert torch.equal(table, want)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total", [(2, 48), (3, 7), (4, 3)])
+def test_chain_checksum_gather(world, total):
+    """The 5-chain's checksum table: each rank's block of rows (unequal blocks,
+    empty ones) reaches every rank in image order."""
+    mp.spawn(_gather_worker, args=(world, _free_port(), total), nprocs=world, join=True)
+
+
 def test_two_gloo_ranks_shard_dcn_like_one_rank():
     port = _free_port()
     mp.spawn(_worker, args=(2, port), nprocs=2, join=True)
@@ -73,3 +100,18 @@ def test_shard_blocks_match_bench_image_seeds():
     for k in ("x", "off", "mask"):
         assert torch.equal(part[k], whole[k][3:5])
     assert torch.equal(part["w"], whole["w"])
+
+
+def test_chain_blocks_match_world_one_images():
+    """A rank's block of the 5-chain regenerates exactly the same images (MSDA
+    camera slices and DCN images) as the world-1 run, and shares its weight."""
+    import bench
+    whole_m, whole_d = bench.chain_inputs(0, 3, SEED, "cpu")
+    part_m, part_d = bench.chain_inputs(1, 2, SEED, "cpu")
+    for k in ("value", "loc", "attn"):
+        assert torch.equal(part_m[k], whole_m[k][1:3])
+    for k in ("shapes", "lsi"):
+        assert torch.equal(part_m[k], whole_m[k])
+    for k in ("x", "off", "mask"):
+        assert torch.equal(part_d[k], whole_d[k][1:3])
+    assert torch.equal(part_d["w"], whole_d["w"])
