@@ -365,8 +365,9 @@ BEVK_API int bevk_ms_deform_attn_forward(const void *value, const int64_t *spati
                                          int num_point, int im2col_step, void *output, int dtype,
                                          bevk_stream_t stream) {
   clear_error();
-  if (!value || !spatial_shapes || !level_start_index || !sampling_loc || !attention_weights ||
-      !output)
+  // the per-query arrays are empty (and may be NULL) when num_query == 0
+  if (!value || !spatial_shapes || !level_start_index ||
+      (num_query != 0 && (!sampling_loc || !attention_weights || !output)))
     return fail(BEVK_ERR_INVALID_ARGUMENT, "ms_deform_attn_forward: null pointer");
   if (batch <= 0 || spatial_size <= 0 || num_heads <= 0 || channels <= 0 || num_levels <= 0 ||
       num_query < 0 || num_point <= 0)
@@ -479,8 +480,10 @@ BEVK_API int bevk_ms_deform_attn_backward(const void *value, const int64_t *spat
                                           void *workspace, size_t workspace_bytes, int dtype,
                                           bevk_stream_t stream) {
   clear_error();
-  if (!value || !spatial_shapes || !level_start_index || !sampling_loc || !attention_weights ||
-      !grad_output || !grad_value || !grad_sampling_loc || !grad_attention_weights)
+  // the per-query arrays are empty (and may be NULL) when num_query == 0
+  const bool per_query_ok = num_query == 0 || (sampling_loc && attention_weights && grad_output &&
+                                               grad_sampling_loc && grad_attention_weights);
+  if (!value || !spatial_shapes || !level_start_index || !grad_value || !per_query_ok)
     return fail(BEVK_ERR_INVALID_ARGUMENT, "ms_deform_attn_backward: null pointer");
   if (batch <= 0 || spatial_size <= 0 || num_heads <= 0 || channels <= 0 || num_levels <= 0 ||
       num_query < 0 || num_point <= 0)

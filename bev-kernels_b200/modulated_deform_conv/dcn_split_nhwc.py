@@ -90,7 +90,7 @@ def _forward_nhwc(x_nhwc, w_off, b_off, weight, bias, stride, padding, dilation,
     bias = None if bias is None else bias.to(x_nhwc.dtype)
     relu = bn_scale is not None and bool(act_relu)
     out = torch.empty(B, Ho, Wo, Cout, device=x_nhwc.device, dtype=x_nhwc.dtype)
-    if gemm_offset and offset_conv_supported(x_nhwc, (kH, kW)):
+    if gemm_offset and B > 0 and offset_conv_supported(x_nhwc, (kH, kW)):
         # [B, 3T, Ho, Wo] view of the [B, Ho, Wo, 3T] offset-conv output
         y = offset_conv(x_nhwc, w_off, b_off, stride, padding, dilation).permute(0, 3, 1, 2)
     else:
@@ -151,6 +151,12 @@ class DCNSplitNHWCFunction(torch.autograd.Function):
         st, pd, dl = ctx.stride, ctx.padding, ctx.dilation
         Cout, _, kH, kW = weight.shape
         B, H, W, Cin = x.shape
+        if B == 0:
+            # an empty batch: zero gradients
+            return (torch.zeros_like(x), torch.zeros_like(w_off),
+                    torch.zeros(w_off.shape[0], device=x.device, dtype=w_off.dtype),
+                    torch.zeros_like(weight), torch.zeros(Cout, device=x.device, dtype=x.dtype)
+                    if ctx.with_bias else None, None, None, None, None, None, None)
         T = kH * kW
         Ho = out_size(H, pd, dl, kH, st)
         Wo = out_size(W, pd, dl, kW, st)

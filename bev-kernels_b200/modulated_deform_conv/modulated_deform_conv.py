@@ -163,6 +163,8 @@ def dcn_forward_into(input, offset, mask, weight, bias, output, stride, padding,
     ``mask_is_logit`` applies the sigmoid on load (raw offset-conv output);
     ``act_relu`` applies max(0, .) in the kernel's epilogue.
     """
+    if input.shape[0] == 0:
+        return output  # an empty batch: nothing to compute or write
     kh, kw = weight.shape[2], weight.shape[3]
     sh, sw = _pair(stride)
     ph, pw = _pair(padding)
@@ -325,6 +327,15 @@ def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dila
     ext = _load_ext()
     B, C, H, W = input.shape
     Cout, Cg, kH, kW = weight.shape
+    if B == 0:
+        # an empty batch: zero gradients of the requested inputs
+        acc0 = torch.float64 if input.dtype == torch.float64 else torch.float32
+        return (torch.zeros_like(input) if need_input else None,
+                torch.zeros_like(offset) if need_offset_mask else None,
+                torch.zeros_like(mask) if need_offset_mask else None,
+                torch.zeros_like(weight) if need_weight else None,
+                torch.zeros(Cout, device=input.device, dtype=acc0).to(input.dtype)
+                if need_bias else None)
     T = kH * kW
     sh, sw = _pair(stride)
     ph, pw = _pair(padding)

@@ -390,7 +390,9 @@ BEVK_API int bevk_dcn_backward_data(const bevk_dcn_backward_data_args *args,
  * (batch % min(batch, im2col_step) == 0, else BEVK_ERR_INVALID_ARGUMENT)
  * but the whole batch runs in one launch.  value, sampling_loc,
  * attention_weights and output share dtype (f32, f16 or bf16; f16/bf16
- * accumulate in fp32).  Every output element is written.
+ * accumulate in fp32).  Every output element is written.  num_query may be 0
+ * (sampling_loc, attention_weights and output are then empty and may be
+ * NULL).
  */
 BEVK_API int bevk_ms_deform_attn_forward(
     const void *value, const int64_t *spatial_shapes,
@@ -425,7 +427,9 @@ BEVK_API size_t bevk_ms_deform_attn_backward_workspace_bytes(int batch, int spat
  * and grad_attention_weights [..., num_point] are written for every sample
  * (zeros for samples outside the bilinear gate).  im2col_step as in the
  * forward.  grad_value accumulation uses floating-point atomics, so its
- * last bits vary from run to run, as in the reference.
+ * last bits vary from run to run, as in the reference.  num_query may be 0
+ * (the per-query arrays are then empty and may be NULL; grad_value is left
+ * as it is for f32 and written with zeros for f16/bf16).
  */
 BEVK_API int bevk_ms_deform_attn_backward(
     const void *value, const int64_t *spatial_shapes,

@@ -217,3 +217,28 @@ def test_errors_are_raised(cuda):
         modulated_deform_conv2d(x, off[:, :10], mask, w, b, 1, 1, 1)      # wrong offset channels
     with pytest.raises(RuntimeError):
         modulated_deform_conv2d(x, off, mask, w, b, 1, 1, 1, 3, 1)        # groups must divide
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16], ids=["f32", "f16"])
+def test_empty_batch(cuda, dt):
+    """A batch of zero images gives an empty output and zero gradients, through
+    the NCHW Function and through the Pack module (the NHWC split path)."""
+    import modulated_deform_conv as mdc
+    x = torch.zeros(0, 16, 8, 9, device=cuda, dtype=dt, requires_grad=True)
+    off = torch.zeros(0, 18, 8, 9, device=cuda, dtype=dt, requires_grad=True)
+    mask = torch.zeros(0, 9, 8, 9, device=cuda, dtype=dt, requires_grad=True)
+    w = torch.randn(24, 16, 3, 3, device=cuda, dtype=dt, requires_grad=True)
+    b = torch.randn(24, device=cuda, dtype=dt, requires_grad=True)
+    out = mdc.modulated_deform_conv2d(x, off, mask, w, b, 1, 1, 1)
+    assert out.shape == (0, 24, 8, 9) and out.dtype == dt
+    out.sum().backward()
+    assert x.grad.shape == x.shape and off.grad.shape == off.shape and mask.grad.shape == mask.shape
+    assert not torch.count_nonzero(w.grad) and not torch.count_nonzero(b.grad)
+    m = mdc.ModulatedDeformConv2dPack(16, 24, 3, padding=1).to(cuda, dt)
+    xp = torch.zeros(0, 16, 8, 9, device=cuda, dtype=dt, requires_grad=True)
+    y = m(xp)
+    assert y.shape == (0, 24, 8, 9)
+    y.sum().backward()
+    assert xp.grad.shape == xp.shape
+    assert not torch.count_nonzero(m.weight.grad) and not torch.count_nonzero(m.bias.grad)
+    assert not torch.count_nonzero(m.conv_offset.weight.grad)

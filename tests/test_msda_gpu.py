@@ -166,3 +166,20 @@ def test_backward_im2col_step_contract(cuda):
     value, shapes, lsi, loc, attn, gout = _bwd_case(cuda, cfg, torch.float32)
     with pytest.raises(RuntimeError, match="im2col_step"):
         ms_deform_attn.ms_deform_attn_backward(value, shapes, lsi, loc, attn, gout, im2col_step=2)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16], ids=["f32", "f16"])
+def test_zero_queries(cuda, dt):
+    """num_query = 0: an empty output, zero grad_value and empty location /
+    attention gradients."""
+    import ms_deform_attn
+    value, shapes, lsi, loc, attn = msda_inputs(3, 2, [(6, 7), (3, 4)], 8, 32, 0, 4)
+    value, loc, attn = (t.to(cuda, dt) for t in (value, loc, attn))
+    shapes, lsi = shapes.to(cuda), lsi.to(cuda)
+    out = ms_deform_attn.ms_deform_attn_forward(value, shapes, lsi, loc, attn)
+    assert out.shape == (2, 0, 256) and out.dtype == dt
+    gout = torch.zeros(2, 0, 256, device=cuda, dtype=dt)
+    gv, gl, ga = ms_deform_attn.ms_deform_attn_backward(value, shapes, lsi, loc, attn, gout)
+    torch.cuda.synchronize()
+    assert gv.shape == value.shape and not torch.count_nonzero(gv)
+    assert gl.shape == loc.shape and ga.shape == attn.shape
