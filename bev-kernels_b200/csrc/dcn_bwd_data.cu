@@ -667,27 +667,33 @@ int launch_dcn_backward_data(const bevk_dcn_backward_data_args *a, const DcnDims
   if (need_x)
     ok = ok && pr.input_strides[1] == 1 && mult(pr.input_strides[0]) &&
          mult(pr.input_strides[2]) && mult(pr.input_strides[3]) && aligned(input, 16);
-  if (need_dcol)
-    ok = ok && mult(a->dcol_ld) && aligned(dcol, 16) &&
-         static_cast<uint64_t>(d.M) * static_cast<uint64_t>(a->dcol_ld) <= 0xFFFFFFFFull;
+  if (need_dcol) ok = ok && mult(a->dcol_ld) && aligned(dcol, 16);
   if (col != nullptr) ok = ok && mult(a->col_ld) && aligned(col, 16);
   if (grad_input != nullptr) {
     const int64_t *g = a->grad_input_strides;
     ok = ok && g[1] == 1 && mult(g[0]) && mult(g[2]) && mult(g[3]) && aligned(grad_input, 16);
   }
-  // 32-bit offsets of a pixel's channel vector inside one image
-  if (need_x)
-    ok = ok && (static_cast<int64_t>(d.H) - 1) * pr.input_strides[2] +
-                       (static_cast<int64_t>(d.W) - 1) * pr.input_strides[3] + d.Cin <=
-                   0x7FFFFFFF;
   if (!ok)
     return fail(BEVK_ERR_UNSUPPORTED,
                 "dcn backward data: needs channel-contiguous input / gradient, channels and "
                 "row strides in whole 16-byte vectors, 16-byte-aligned pointers");
+  // 32-bit indices: bucket entries hold 32-bit dcol row offsets, a pixel's
+  // channel vector inside one image is a 32-bit offset, and the sort counts
+  // (4 corners per sample) fit an int
   const int64_t nb = static_cast<int64_t>(d.B) * d.dg * d.H * d.W;
   const int64_t units = d.M * d.dg * d.T;
+  if (need_dcol && static_cast<uint64_t>(d.M) * static_cast<uint64_t>(a->dcol_ld) > 0xFFFFFFFFull)
+    return fail(BEVK_ERR_INDEX_OVERFLOW,
+                "dcn backward data: column gradient of %lld rows x %lld elements exceeds "
+                "32-bit offsets", static_cast<long long>(d.M), static_cast<long long>(a->dcol_ld));
+  if (need_x && (static_cast<int64_t>(d.H) - 1) * pr.input_strides[2] +
+                        (static_cast<int64_t>(d.W) - 1) * pr.input_strides[3] + d.Cin >
+                    0x7FFFFFFF)
+    return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn backward data: one input image exceeds 32-bit offsets");
   if (nb + 1 > 0x7FFFFFFF || 4 * units > 0x7FFFFFFF)
-    return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn backward data: too many samples");
+    return fail(BEVK_ERR_INDEX_OVERFLOW,
+                "dcn backward data: %lld samples (4 corners each) exceed 32-bit counts",
+                static_cast<long long>(units));
   if (grad_input != nullptr &&
       (workspace == nullptr || workspace_bytes < dcn_backward_data_workspace_bytes(d)))
     return fail(BEVK_ERR_WORKSPACE, "dcn backward data: workspace of %zu bytes, %zu needed",

@@ -427,7 +427,8 @@ void dcn_col2im(const Tensor &dcol, const c10::optional<Tensor> &input, const Te
 // input / offset / mask / gradients in any memory format (an NHWC tensor is
 // passed as its permuted view), NHWC column matrices [M, kH*kW*C] with unit
 // column stride.  Returns false, having written nothing, when the layouts are
-// not the channel-contiguous 16-byte-vector ones the kernels need.
+// not the channel-contiguous 16-byte-vector ones the kernels need or the
+// problem exceeds their 32-bit indices.
 bool dcn_backward_data(const c10::optional<Tensor> &dcol, const c10::optional<Tensor> &input,
                        const Tensor &offset, const Tensor &mask, bool mask_is_logit,
                        int64_t in_channels, int64_t height, int64_t width, int64_t kernel_h,
@@ -510,7 +511,9 @@ bool dcn_backward_data(const c10::optional<Tensor> &dcol, const c10::optional<Te
                                         ptr(gi), ptr(go), ptr(gm), ptr(cl), ptr(ws),
                                         ws.defined() ? static_cast<size_t>(ws.numel()) : 0,
                                         current_stream(offset));
-  if (st == BEVK_ERR_UNSUPPORTED) return false;
+  // layouts or sizes this entry point does not cover: the caller takes the
+  // general scatter path (any strides, 64-bit indices)
+  if (st == BEVK_ERR_UNSUPPORTED || st == BEVK_ERR_INDEX_OVERFLOW) return false;
   check_status(st, "dcn_backward_data");
   return true;
 }

@@ -369,7 +369,10 @@ BEVK_API size_t bevk_dcn_backward_data_workspace_bytes(const bevk_dcn_problem *p
  * may vary between runs.  Layouts: input channel stride 1 (when read),
  * grad_input channel stride 1, C / (C / deformable_groups) / the row strides
  * whole 16-byte vectors, 16-byte-aligned pointers; otherwise
- * BEVK_ERR_UNSUPPORTED (bevk_dcn_col2im + bevk_dcn_columns cover any layout).
+ * BEVK_ERR_UNSUPPORTED.  Sizes: M * dcol_ld below 2^32, one input image
+ * below 2^31 elements, 4 * M * deformable_groups * kH * kW below 2^31;
+ * otherwise BEVK_ERR_INDEX_OVERFLOW.  (bevk_dcn_col2im + bevk_dcn_columns
+ * cover any layout and size.)
  */
 BEVK_API int bevk_dcn_backward_data(const bevk_dcn_backward_data_args *args,
                                     const void *input, const void *offset, const void *mask,

@@ -111,3 +111,31 @@ def test_msda_im2col_step_contract():
     st = lib.bevk_ms_deform_attn_forward(None, None, None, None, None, 3, 100, 8, 32, 1, 10, 4,
                                          64, None, cabi.DTYPE_F32, None)
     assert st == cabi.ERR_INVALID_ARGUMENT
+
+
+def test_backward_data_size_limits_without_device():
+    """bevk_dcn_backward_data rejects problems past its 32-bit indices with
+    BEVK_ERR_INDEX_OVERFLOW before touching the device, and sizes the
+    workspace of any problem."""
+    lib = cabi.lib()
+    B, C, H, W = 64, 16, 1000, 1000          # 64 M pixels x 9 taps: 2.3 G corner entries
+    a = cabi.DcnBackwardDataArgs()
+    a.problem = _problem(batch=B, in_channels=C, out_channels=C, height=H, width=W)
+    for i, v in enumerate((H * W * C, 1, W * C, C)):           # NHWC input
+        a.problem.input_strides[i] = v
+        a.grad_input_strides[i] = v
+    for i, v in enumerate((18 * H * W, H * W, W, 1)):
+        a.problem.offset_strides[i] = v
+        a.grad_offset_strides[i] = v
+    for i, v in enumerate((9 * H * W, H * W, W, 1)):
+        a.problem.mask_strides[i] = v
+        a.grad_mask_strides[i] = v
+    a.grad_dtype = cabi.DTYPE_F16
+    a.dcol_ld = a.col_ld = 9 * C
+    nbytes = lib.bevk_dcn_backward_data_workspace_bytes(ctypes.byref(a.problem))
+    assert nbytes >= 4 * B * H * W * 9 * 8
+    fake = 256  # 16-byte aligned, never dereferenced: the size checks come first
+    st = lib.bevk_dcn_backward_data(ctypes.byref(a), fake, fake, fake, fake, fake, fake, fake,
+                                    fake, fake, nbytes, None)
+    assert st == cabi.ERR_INDEX_OVERFLOW, (st, cabi.last_error())
+    assert "32-bit" in cabi.last_error()
