@@ -242,3 +242,51 @@ def test_empty_batch(cuda, dt):
     assert xp.grad.shape == xp.shape
     assert not torch.count_nonzero(m.weight.grad) and not torch.count_nonzero(m.bias.grad)
     assert not torch.count_nonzero(m.conv_offset.weight.grad)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16], ids=["f32_simt", "f16_tc"])
+def test_sampling_on_gate_and_edges(cuda, dt):
+    """Sampling positions exactly on the bilinear gate and the image edges
+    (h or w = -1, -0.5, 0, H-1, H-0.5, H and between): samples at -1 or H are
+    dropped, corners outside [0, H-1] x [0, W-1] count as zero -- the
+    oracle's semantics, through the exact SIMT path (fp32) and the
+    tensor-core path (fp16, forward and backward)."""
+    import modulated_deform_conv as mdc
+    B, C, H, W, Cout = 1, 32, 6, 7, 32
+    g = torch.Generator().manual_seed(91)
+    x = torch.randn(B, C, H, W, generator=g)
+    w = torch.randn(Cout, C, 3, 3, generator=g) * 0.1
+    b = torch.randn(Cout, generator=g)
+    mask = torch.sigmoid(torch.randn(B, 9, H, W, generator=g))
+    targets_h = [-1.0, -0.5, 0.0, 0.25, H - 1.0, H - 0.5, float(H), 2.75]
+    targets_w = [float(W), -1.0, W - 0.5, -0.5, 0.0, W - 1.0, 3.5, 0.75, 1.0]
+    off = torch.zeros(B, 18, H, W)
+    n = 0
+    for oh in range(H):
+        for ow in range(W):
+            for t in range(9):
+                ki, kj = divmod(t, 3)
+                off[0, 2 * t, oh, ow] = targets_h[n % len(targets_h)] - (oh - 1 + ki)
+                off[0, 2 * t + 1, oh, ow] = targets_w[n % len(targets_w)] - (ow - 1 + kj)
+                n += 1
+    xs, offs, masks, ws, bs = (t.to(dt) for t in (x, off, mask, w, b))
+    # every target is exact in fp16, so both dtypes sample the same positions
+    assert torch.equal(offs.float(), off)
+    want = _oracle(xs, offs, masks, ws, bs, 1, 1, 1)
+    tens = [xs.to(cuda), offs.to(cuda).requires_grad_(), masks.to(cuda).requires_grad_(),
+            ws.to(cuda), bs.to(cuda)]
+    if dt == torch.float16:
+        tens[0] = tens[0].contiguous(memory_format=torch.channels_last)
+    tens[0].requires_grad_()
+    out = mdc.modulated_deform_conv2d(*tens, 1, 1, 1)
+    o = out.detach()
+    if dt == torch.float32:
+        assert rel_l2(o, want) <= FP32_REL and max_abs(o, want) <= FP32_ABS
+    else:
+        assert rel_l2(o, want) <= HALF_REL
+    gout = torch.randn(out.shape, generator=torch.Generator().manual_seed(92)).to(dt)
+    out.backward(gout.to(cuda))
+    gw = oracle.dcn_backward(*(t.float().numpy() for t in (xs, offs, masks, ws, gout)), 1, 1, 1)
+    tol = FP32_REL if dt == torch.float32 else HALF_REL
+    for t, ref, name in zip(tens[:3], gw[:3], ("x", "offset", "mask")):
+        assert rel_l2(t.grad, torch.from_numpy(ref)) <= tol, (name, rel_l2(t.grad, torch.from_numpy(ref)))
