@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -42,6 +43,14 @@ int current_device() {
   int d = -1;
   if (cudaGetDevice(&d) != cudaSuccess) return -1;
   return d;
+}
+
+bool programmatic_launch_enabled() {
+  static const bool on = [] {
+    const char *v = std::getenv("BEVK_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 const DeviceInfo &device_info(int device) {

@@ -31,6 +31,11 @@ struct DeviceInfo {
 const DeviceInfo &device_info(int device);
 int current_device();
 
+// Whether kernels that support it are launched as programmatic dependents of
+// the stream's previous kernel (on unless the environment sets BEVK_PDL=0;
+// read once).
+bool programmatic_launch_enabled();
+
 inline size_t dtype_size(int dtype) {
   switch (dtype) {
     case BEVK_DTYPE_F32: return 4;

@@ -19,6 +19,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// ---------------------------------------------------------------- dependent launch
+// Programmatic dependent launch.  launch_dependents lets the stream's next
+// kernel (launched with cudaLaunchAttributeProgrammaticStreamSerialization)
+// place its CTAs once every CTA of this grid has issued it or exited;
+// wait_prerequisites blocks until the previous kernel of the stream has
+// completed and its memory writes are visible.  Both are no-ops in a launch
+// without that attribute.  A kernel reads or writes no global memory that
+// another kernel may touch before its wait.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_wait_prerequisites() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

@@ -331,6 +331,10 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   const int n0 = NSPLIT ? n_tile * 2 * BN + static_cast<int>(cr) * BN : n_tile * BN;
   const int g_row0 = NSPLIT ? static_cast<int>(cr) * kGRows : 0;  // first tile row gathered here
 
+  // The prologue below (barriers, TMEM, descriptor prefetch) touches no
+  // global memory, so under a programmatic launch it overlaps the previous
+  // kernel's tail; the next kernel may be placed as soon as SMs free up.
+  ptx::grid_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       // gather warps (of both CTAs when paired) + the TMA arrive with bytes
@@ -354,6 +358,8 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
     }
   }
   if (warp == R::kTma && lane == 0) ptx::tma_prefetch_desc(&tmap_w);
+  // every global read (input, offsets, mask, weights, bias) and write comes after
+  ptx::grid_wait_prerequisites();
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -788,10 +794,25 @@ int launch_tc(const TcParams &p, const CUtensorMap &tmap, const void *x, const v
   if (attr_err[dev] != cudaSuccess)
     return fail(BEVK_ERR_CUDA, "dcn tc: cudaFuncSetAttribute: %s",
                 cudaGetErrorString(attr_err[dev]));
-  kern<<<ctas, tc_threads<MODE>(), L::kAlloc, stream>>>(tmap, p, static_cast<const T *>(x),
-                                               static_cast<const T *>(off),
-                                               static_cast<const T *>(msk),
-                                               static_cast<const T *>(bias), static_cast<T *>(y));
+  // Programmatic dependent launch: the kernel's prologue overlaps the tail of
+  // the stream's previous kernel; it waits for that kernel (griddepcontrol)
+  // before touching global memory.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+  cfg.blockDim = dim3(tc_threads<MODE>());
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = programmatic_launch_enabled() ? 1 : 0;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, tmap, p, static_cast<const T *>(x),
+                                             static_cast<const T *>(off),
+                                             static_cast<const T *>(msk),
+                                             static_cast<const T *>(bias), static_cast<T *>(y));
+  if (err != cudaSuccess)
+    return fail(BEVK_ERR_CUDA, "dcn_fwd_tc_kernel launch: %s", cudaGetErrorString(err));
   return check_launch("dcn_fwd_tc_kernel");
 }
 
