@@ -39,6 +39,14 @@ int check_launch(const char *what) {
   return BEVK_OK;
 }
 
+int launched(cudaError_t launch_result, const char *what) {
+  if (launch_result != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail(BEVK_ERR_CUDA, "%s: %s", what, cudaGetErrorString(launch_result));
+  }
+  return check_launch(what);
+}
+
 int current_device() {
   int d = -1;
   if (cudaGetDevice(&d) != cudaSuccess) return -1;

@@ -19,6 +19,9 @@ const char *last_error();
 
 // Maps a CUDA error from the most recent launch into a status.
 int check_launch(const char *what);
+// Maps the result of a cudaLaunchKernelEx (then any pending launch error)
+// into a status.
+int launched(cudaError_t launch_result, const char *what);
 
 // Cached per-device properties (filled once per device, thread-safe).
 struct DeviceInfo {
@@ -35,6 +38,26 @@ int current_device();
 // the stream's previous kernel (on unless the environment sets BEVK_PDL=0;
 // read once).
 bool programmatic_launch_enabled();
+
+// Launches `kern` (grid, block, dynamic shared memory, stream) as a
+// programmatic dependent of the stream's previous kernel when that is
+// enabled.  The kernel calls ptx::grid_wait_prerequisites() before it touches
+// global memory, so results are as with an ordinary launch.
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = programmatic_launch_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args &&>(args)...);
+}
 
 inline size_t dtype_size(int dtype) {
   switch (dtype) {

@@ -44,6 +44,7 @@
 #include <type_traits>
 
 #include "bevk_internal.h"
+#include "bevk_ptx.cuh"
 
 namespace bevk {
 namespace {
@@ -206,6 +207,8 @@ __device__ __forceinline__ int corner_bucket(const BwdDataParams &p, const Sampl
 template <typename T>
 __global__ void __launch_bounds__(256)
 dcn_bwd_count_kernel(const BwdDataParams p, const T *__restrict__ off, int *__restrict__ cnt) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   const int units = static_cast<int>(p.units);
   for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < units; u += gridDim.x * blockDim.x) {
     const Sample s = sample_at(p, off, u);
@@ -226,6 +229,8 @@ constexpr int kScanThreads = 1024, kScanItems = 8;
 // aligned and tiles start at multiples of 8192).
 __global__ void __launch_bounds__(kScanThreads)
 dcn_bwd_scan_kernel(int *__restrict__ cnt, int nb) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   __shared__ int warp_sum[kScanThreads / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int carry = 0;
@@ -288,6 +293,8 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 dcn_bwd_fill_kernel(const BwdDataParams p, const T *__restrict__ off, const T *__restrict__ msk,
                     int *__restrict__ ends, uint2 *__restrict__ entries) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   const int units = static_cast<int>(p.units);
   for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < units; u += gridDim.x * blockDim.x) {
     const Sample s = sample_at(p, off, u);
@@ -338,6 +345,8 @@ dcn_bwd_sample_kernel(const BwdDataParams p, const T *__restrict__ x, const T *_
                       const T *__restrict__ msk, const T *__restrict__ dcol,
                       TG *__restrict__ goff, TG *__restrict__ gmask, T *__restrict__ col, int tpw,
                       int ngroups) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   constexpr int V = 16 / sizeof(T);
   const int lane = threadIdx.x & 31;
   const int unit = blockIdx.x * kSampleWarps + (threadIdx.x >> 5);
@@ -497,6 +506,8 @@ __global__ void __launch_bounds__(kGatherThreads, 8)
 dcn_bwd_gradx_kernel(const BwdDataParams p, const T *__restrict__ dcol,
                      const int *__restrict__ starts, const uint2 *__restrict__ entries,
                      TG *__restrict__ gx, int lpg_log2, int nchunks) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   constexpr int V = 16 / sizeof(T);
   // entries per batch: loads in flight per lane = kUnroll * VPL, with the
   // register budget of eight CTAs per SM
@@ -588,18 +599,21 @@ int launch_typed(const BwdDataParams &p, const void *input, const void *offset,
         cudaSuccess)
       return check_launch("dcn backward data: bucket count reset");
     const int64_t blocks = std::min<int64_t>((p.units + 255) / 256, max_blocks);
-    dcn_bwd_count_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p, off, cnt);
-    int st = check_launch("dcn_bwd_count_kernel");
+    int st = launched(launch_dependent(dcn_bwd_count_kernel<T>, dim3(static_cast<unsigned>(blocks)),
+                                       dim3(256), 0, stream, p, off, cnt),
+                      "dcn_bwd_count_kernel");
     if (st != BEVK_OK) return st;
-    dcn_bwd_scan_kernel<<<1, kScanThreads, 0, stream>>>(cnt, p.nb);
-    st = check_launch("dcn_bwd_scan_kernel");
+    st = launched(launch_dependent(dcn_bwd_scan_kernel, dim3(1), dim3(kScanThreads), 0, stream,
+                                   cnt, p.nb),
+                  "dcn_bwd_scan_kernel");
     if (st != BEVK_OK) return st;
   }
   if (grad_input != nullptr) {
     const int64_t fblocks = std::min<int64_t>((p.units + 255) / 256, max_blocks);
-    dcn_bwd_fill_kernel<T><<<static_cast<unsigned>(fblocks), 256, 0, stream>>>(
-        p, off, static_cast<const T *>(mask), cnt, entries);
-    int st = check_launch("dcn_bwd_fill_kernel");
+    int st = launched(launch_dependent(dcn_bwd_fill_kernel<T>, dim3(static_cast<unsigned>(fblocks)),
+                                       dim3(256), 0, stream, p, off,
+                                       static_cast<const T *>(mask), cnt, entries),
+                      "dcn_bwd_fill_kernel");
     if (st != BEVK_OK) return st;
     // The gather runs before the sample kernel, while the column gradient
     // (written just before this call) is still in L2.  Lanes per bucket:
@@ -617,10 +631,12 @@ int launch_typed(const BwdDataParams &p, const void *input, const void *offset,
     if (gblocks > 0x7FFFFFFF)
       return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn backward data: grid too large");
     auto kern = vpl == 2 ? dcn_bwd_gradx_kernel<T, TG, 2> : dcn_bwd_gradx_kernel<T, TG, 1>;
-    kern<<<static_cast<unsigned>(gblocks), kGatherThreads, 0, stream>>>(
-        p, static_cast<const T *>(dcol), cnt, entries, static_cast<TG *>(grad_input), lpg_log2,
-        nchunks);
-    st = check_launch("dcn_bwd_gradx_kernel");
+    st = launched(launch_dependent(kern, dim3(static_cast<unsigned>(gblocks)),
+                                   dim3(kGatherThreads), 0, stream, p,
+                                   static_cast<const T *>(dcol), static_cast<const int *>(cnt),
+                                   static_cast<const uint2 *>(entries),
+                                   static_cast<TG *>(grad_input), lpg_log2, nchunks),
+                  "dcn_bwd_gradx_kernel");
     if (st != BEVK_OK) return st;
   }
   if (grad_offset == nullptr && grad_mask == nullptr && col == nullptr) return BEVK_OK;
@@ -631,11 +647,13 @@ int launch_typed(const BwdDataParams &p, const void *input, const void *offset,
   const int64_t warps = p.M * p.dg * ngroups;
   if (warps > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn backward data: grid too large");
   const int64_t blocks = (warps + kSampleWarps - 1) / kSampleWarps;
-  dcn_bwd_sample_kernel<T, TG><<<static_cast<unsigned>(blocks), kSampleWarps * 32, 0, stream>>>(
-      p, static_cast<const T *>(input), off, static_cast<const T *>(mask),
-      static_cast<const T *>(dcol), static_cast<TG *>(grad_offset),
-      static_cast<TG *>(grad_mask), static_cast<T *>(col), tpw, ngroups);
-  return check_launch("dcn_bwd_sample_kernel");
+  return launched(launch_dependent(dcn_bwd_sample_kernel<T, TG>, dim3(static_cast<unsigned>(blocks)),
+                                   dim3(kSampleWarps * 32), 0, stream, p,
+                                   static_cast<const T *>(input), off,
+                                   static_cast<const T *>(mask), static_cast<const T *>(dcol),
+                                   static_cast<TG *>(grad_offset), static_cast<TG *>(grad_mask),
+                                   static_cast<T *>(col), tpw, ngroups),
+                  "dcn_bwd_sample_kernel");
 }
 
 }  // namespace

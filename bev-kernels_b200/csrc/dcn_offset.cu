@@ -24,6 +24,7 @@
 #include <cstdint>
 
 #include "bevk_internal.h"
+#include "bevk_ptx.cuh"
 
 namespace bevk {
 namespace {
@@ -53,6 +54,8 @@ __global__ void __launch_bounds__(256) dcn_offset_sum_kernel(const SumParams p,
                                                              const float *__restrict__ z,
                                                              const float *__restrict__ bias,
                                                              T *__restrict__ y) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.total; i += gridDim.x * blockDim.x) {
     const int m = i / p.c3;
     const int c = i - m * p.c3;
@@ -107,15 +110,17 @@ int launch_dcn_offset_sum(const bevk_dcn_problem *pr, const DcnDims &d, const fl
   const int grid = static_cast<int>(want < cap ? want : cap);
   switch (pr->dtype) {
     case BEVK_DTYPE_F16:
-      dcn_offset_sum_kernel<__half><<<grid, 256, 0, stream>>>(p, z, bias, static_cast<__half *>(y));
-      break;
+      return launched(launch_dependent(dcn_offset_sum_kernel<__half>, dim3(grid), dim3(256), 0,
+                                       stream, p, z, bias, static_cast<__half *>(y)),
+                      "dcn_offset_sum_kernel");
     case BEVK_DTYPE_BF16:
-      dcn_offset_sum_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-          p, z, bias, static_cast<__nv_bfloat16 *>(y));
-      break;
+      return launched(launch_dependent(dcn_offset_sum_kernel<__nv_bfloat16>, dim3(grid), dim3(256),
+                                       0, stream, p, z, bias, static_cast<__nv_bfloat16 *>(y)),
+                      "dcn_offset_sum_kernel");
     case BEVK_DTYPE_F32:
-      dcn_offset_sum_kernel<float><<<grid, 256, 0, stream>>>(p, z, bias, static_cast<float *>(y));
-      break;
+      return launched(launch_dependent(dcn_offset_sum_kernel<float>, dim3(grid), dim3(256), 0,
+                                       stream, p, z, bias, static_cast<float *>(y)),
+                      "dcn_offset_sum_kernel");
     default:
       return fail(BEVK_ERR_UNSUPPORTED, "dcn offset sum: dtype %d", pr->dtype);
   }

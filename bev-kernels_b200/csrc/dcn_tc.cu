@@ -797,23 +797,12 @@ int launch_tc(const TcParams &p, const CUtensorMap &tmap, const void *x, const v
   // Programmatic dependent launch: the kernel's prologue overlaps the tail of
   // the stream's previous kernel; it waits for that kernel (griddepcontrol)
   // before touching global memory.
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(ctas));
-  cfg.blockDim = dim3(tc_threads<MODE>());
-  cfg.dynamicSmemBytes = L::kAlloc;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = programmatic_launch_enabled() ? 1 : 0;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, tmap, p, static_cast<const T *>(x),
-                                             static_cast<const T *>(off),
-                                             static_cast<const T *>(msk),
-                                             static_cast<const T *>(bias), static_cast<T *>(y));
-  if (err != cudaSuccess)
-    return fail(BEVK_ERR_CUDA, "dcn_fwd_tc_kernel launch: %s", cudaGetErrorString(err));
-  return check_launch("dcn_fwd_tc_kernel");
+  return launched(launch_dependent(kern, dim3(static_cast<unsigned>(ctas)),
+                                   dim3(tc_threads<MODE>()), L::kAlloc, stream, tmap, p,
+                                   static_cast<const T *>(x), static_cast<const T *>(off),
+                                   static_cast<const T *>(msk), static_cast<const T *>(bias),
+                                   static_cast<T *>(y)),
+                  "dcn_fwd_tc_kernel");
 }
 
 }  // namespace

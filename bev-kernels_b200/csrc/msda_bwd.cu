@@ -34,6 +34,7 @@
 #include <cstdint>
 
 #include "bevk_internal.h"
+#include "bevk_ptx.cuh"
 
 namespace bevk {
 namespace {
@@ -110,6 +111,8 @@ msda_bwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ sha
                     float *__restrict__ grad_value, T *__restrict__ grad_loc,
                     T *__restrict__ grad_attn, int S, int heads, int L, int Q, int P,
                     int64_t n_samples) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   constexpr int C = 32;
   __shared__ int s_lvl[kMaxLevels][3];
   __shared__ BwdGeom s_geo[kBwdWarps][32];
@@ -235,6 +238,8 @@ msda_bwd_generic_kernel(const T *__restrict__ value, const int64_t *__restrict__
                         float *__restrict__ grad_value, T *__restrict__ grad_loc,
                         T *__restrict__ grad_attn, int S, int heads, int C, int L, int Q,
                         int P, int64_t n_samples) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   const int lane = threadIdx.x & 31;
   const int64_t smp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (smp >= n_samples) return;
@@ -289,6 +294,8 @@ msda_bwd_generic_kernel(const T *__restrict__ value, const int64_t *__restrict__
 
 template <typename T>
 __global__ void narrow_kernel(const float *__restrict__ src, T *__restrict__ dst, int64_t n) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     dst[i] = from_f<T>(src[i]);
@@ -322,29 +329,34 @@ int launch_bwd_typed(const void *value, const int64_t *shapes, const int64_t *ls
       const int64_t passes = (n_samples + 31) / 32;
       const int64_t want = (passes + kBwdWarps - 1) / kBwdWarps;
       const int64_t ctas = std::min<int64_t>(want, static_cast<int64_t>(sms > 0 ? sms : 148) * 8);
-      msda_bwd_c32_kernel<T><<<static_cast<unsigned>(ctas), kBwdWarps * 32, 0, stream>>>(
-          static_cast<const T *>(value), shapes, lsi, static_cast<const T *>(loc),
-          static_cast<const T *>(attn), static_cast<const T *>(grad_out), gv,
-          static_cast<T *>(grad_loc), static_cast<T *>(grad_attn), S, heads, L, Q, P, n_samples);
-      const int st = check_launch("msda_bwd_c32_kernel");
+      const int st = launched(
+          launch_dependent(msda_bwd_c32_kernel<T>, dim3(static_cast<unsigned>(ctas)),
+                           dim3(kBwdWarps * 32), 0, stream, static_cast<const T *>(value), shapes,
+                           lsi, static_cast<const T *>(loc), static_cast<const T *>(attn),
+                           static_cast<const T *>(grad_out), gv, static_cast<T *>(grad_loc),
+                           static_cast<T *>(grad_attn), S, heads, L, Q, P, n_samples),
+          "msda_bwd_c32_kernel");
       if (st != BEVK_OK) return st;
     } else {
       const int64_t blocks = (n_samples * 32 + 255) / 256;
       if (blocks > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "msda backward: grid too large");
-      msda_bwd_generic_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-          static_cast<const T *>(value), shapes, lsi, static_cast<const T *>(loc),
-          static_cast<const T *>(attn), static_cast<const T *>(grad_out), gv,
-          static_cast<T *>(grad_loc), static_cast<T *>(grad_attn), S, heads, C, L, Q, P,
-          n_samples);
-      const int st = check_launch("msda_bwd_generic_kernel");
+      const int st = launched(
+          launch_dependent(msda_bwd_generic_kernel<T>, dim3(static_cast<unsigned>(blocks)),
+                           dim3(256), 0, stream, static_cast<const T *>(value), shapes, lsi,
+                           static_cast<const T *>(loc), static_cast<const T *>(attn),
+                           static_cast<const T *>(grad_out), gv, static_cast<T *>(grad_loc),
+                           static_cast<T *>(grad_attn), S, heads, C, L, Q, P, n_samples),
+          "msda_bwd_generic_kernel");
       if (st != BEVK_OK) return st;
     }
   }
   if (!f32 && n_value > 0) {
     const int sms = device_info(current_device()).sm_count;
     const int64_t blocks = std::min<int64_t>((n_value + 255) / 256, static_cast<int64_t>(sms > 0 ? sms : 148) * 16);
-    narrow_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(gv, static_cast<T *>(grad_value), n_value);
-    return check_launch("msda narrow_kernel");
+    return launched(launch_dependent(narrow_kernel<T>, dim3(static_cast<unsigned>(blocks)),
+                                     dim3(256), 0, stream, static_cast<const float *>(gv),
+                                     static_cast<T *>(grad_value), n_value),
+                    "msda narrow_kernel");
   }
   return BEVK_OK;
 }

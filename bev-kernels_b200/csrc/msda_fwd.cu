@@ -108,6 +108,8 @@ msda_fwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ sha
                     const int64_t *__restrict__ lsi, const T *__restrict__ loc,
                     const T *__restrict__ attn, T *__restrict__ out, int S, int heads,
                     int L, int Q, int P, int64_t units) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   using V = Vec4<T>;
   using VT = typename V::type;
   constexpr int C = 32;
@@ -249,6 +251,8 @@ msda_fwd_pass_kernel(const T *__restrict__ value, const int64_t *__restrict__ sh
                      const int64_t *__restrict__ lsi, const T *__restrict__ loc,
                      const T *__restrict__ attn, T *__restrict__ out, int S, int heads, int L,
                      int Q, int P, int64_t passes) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   static_assert(32 % LP == 0, "LP must divide 32");
   constexpr int C = 32;
   constexpr int UPP = 32 / LP;  // units per pass
@@ -408,6 +412,8 @@ msda_fwd_generic_kernel(const T *__restrict__ value, const int64_t *__restrict__
                         const int64_t *__restrict__ lsi, const T *__restrict__ loc,
                         const T *__restrict__ attn, T *__restrict__ out, int S, int heads,
                         int C, int L, int Q, int P, int64_t n) {
+  ptx::grid_launch_dependents();
+  ptx::grid_wait_prerequisites();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int c = static_cast<int>(i % C);
@@ -464,10 +470,11 @@ int launch_pass(const void *value, const int64_t *shapes, const int64_t *lsi, co
   const int sms = device_info(dev).sm_count;
   const int64_t ctas =
       std::min<int64_t>(passes, static_cast<int64_t>(sms > 0 ? sms : 148) * per_sm);
-  kern<<<static_cast<unsigned>(ctas), kPassWarps * 32, 0, stream>>>(
-      static_cast<const T *>(value), shapes, lsi, static_cast<const T *>(loc),
-      static_cast<const T *>(attn), static_cast<T *>(out), S, heads, L, Q, P, passes);
-  return check_launch("msda_fwd_pass_kernel");
+  return launched(launch_dependent(kern, dim3(static_cast<unsigned>(ctas)), dim3(kPassWarps * 32),
+                                   0, stream, static_cast<const T *>(value), shapes, lsi,
+                                   static_cast<const T *>(loc), static_cast<const T *>(attn),
+                                   static_cast<T *>(out), S, heads, L, Q, P, passes),
+                  "msda_fwd_pass_kernel");
 }
 
 template <typename T>
@@ -503,18 +510,21 @@ int launch_typed(const void *value, const int64_t *shapes, const int64_t *lsi, c
   if (fast) {
     const int64_t blocks = (units + kWarps - 1) / kWarps;
     if (blocks > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "msda: grid too large");
-    msda_fwd_c32_kernel<T><<<static_cast<unsigned>(blocks), kWarps * 32, 0, stream>>>(
-        static_cast<const T *>(value), shapes, lsi, static_cast<const T *>(loc),
-        static_cast<const T *>(attn), static_cast<T *>(out), S, heads, L, Q, P, units);
-    return check_launch("msda_fwd_c32_kernel");
+    return launched(launch_dependent(msda_fwd_c32_kernel<T>, dim3(static_cast<unsigned>(blocks)),
+                                     dim3(kWarps * 32), 0, stream, static_cast<const T *>(value),
+                                     shapes, lsi, static_cast<const T *>(loc),
+                                     static_cast<const T *>(attn), static_cast<T *>(out), S,
+                                     heads, L, Q, P, units),
+                    "msda_fwd_c32_kernel");
   }
   const int64_t n = units * C;
   const int64_t blocks = (n + 255) / 256;
   if (blocks > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "msda: grid too large");
-  msda_fwd_generic_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-      static_cast<const T *>(value), shapes, lsi, static_cast<const T *>(loc),
-      static_cast<const T *>(attn), static_cast<T *>(out), S, heads, C, L, Q, P, n);
-  return check_launch("msda_fwd_generic_kernel");
+  return launched(launch_dependent(msda_fwd_generic_kernel<T>, dim3(static_cast<unsigned>(blocks)),
+                                   dim3(256), 0, stream, static_cast<const T *>(value), shapes,
+                                   lsi, static_cast<const T *>(loc), static_cast<const T *>(attn),
+                                   static_cast<T *>(out), S, heads, C, L, Q, P, n),
+                  "msda_fwd_generic_kernel");
 }
 
 }  // namespace
