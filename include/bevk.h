@@ -75,6 +75,15 @@ BEVK_API const char *bevk_last_error_message(void);
  */
 BEVK_API int bevk_device_watchdog(int device, unsigned int *code);
 
+/*
+ * Launch order.  The library's kernels are launched as programmatic
+ * dependents of the stream's previous kernel: their set-up (barriers, tensor
+ * memory, descriptor prefetch) may overlap that kernel's last CTAs, and each
+ * waits for it to complete before reading or writing global memory, so stream
+ * order holds as with ordinary launches.  Setting the environment variable
+ * BEVK_PDL=0 (read once per process) launches them the ordinary way.
+ */
+
 /* ------------------------------------------------------------------------ */
 /* DCNv2 (modulated deformable convolution), forward                        */
 /* ------------------------------------------------------------------------ */
