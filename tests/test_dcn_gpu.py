@@ -290,3 +290,59 @@ def test_sampling_on_gate_and_edges(cuda, dt):
     tol = FP32_REL if dt == torch.float32 else HALF_REL
     for t, ref, name in zip(tens[:3], gw[:3], ("x", "offset", "mask")):
         assert rel_l2(t.grad, torch.from_numpy(ref)) <= tol, (name, rel_l2(t.grad, torch.from_numpy(ref)))
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_back_to_back_layers_read_their_predecessor(cuda, dt):
+    """A chain of layers, each reading the previous launch's output with no
+    synchronisation in between.  Every launch lets the next one start its
+    set-up early (programmatic dependent launch) and waits for its
+    predecessor before touching memory, so the chain equals, bit for bit, the
+    same chain with the device synchronised between layers -- launched
+    eagerly and replayed from a CUDA graph."""
+    import _modulated_deform_conv_ext as ext
+    import modulated_deform_conv as mdc
+    B, C, H, W, L = 2, 256, 29, 50, 6
+    g = torch.Generator(device=cuda).manual_seed(31)
+    x0 = torch.randn(B, C, H, W, device=cuda, generator=g).to(dt).contiguous(
+        memory_format=torch.channels_last)
+    offs = [(torch.randn(B, 18, H, W, device=cuda, generator=g) * 2).to(dt) for _ in range(L)]
+    masks = [torch.rand(B, 9, H, W, device=cuda, generator=g).to(dt) for _ in range(L)]
+    wpk = [mdc.packed_weight((torch.randn(C, C, 3, 3, device=cuda, generator=g)
+                              * (2.0 / (9 * C)) ** 0.5).to(dt)) for _ in range(L)]
+
+    def chain(outs, sync):
+        h = x0
+        for i in range(L):
+            ext.dcn_forward(h, offs[i], masks[i], wpk[i], None, outs[i], 3, 3, 1, 1, 1, 1, 1, 1,
+                            1, 1, False)
+            if sync:
+                torch.cuda.synchronize()
+            h = outs[i]
+
+    want = [torch.empty_like(x0) for _ in range(L)]
+    chain(want, True)
+    assert all(torch.isfinite(o).all() for o in want)
+    got = [torch.full_like(x0, float("nan")) for _ in range(L)]
+    for _ in range(3):
+        for o in got:
+            o.fill_(float("nan"))
+        chain(got, False)
+        torch.cuda.synchronize()
+        assert all(torch.equal(a, b) for a, b in zip(got, want))
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        for o in got:
+            o.fill_(float("nan"))
+        with torch.cuda.graph(graph, stream=side):
+            chain(got, False)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        for o in got:
+            o.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert all(torch.equal(a, b) for a, b in zip(got, want))
+    del graph
