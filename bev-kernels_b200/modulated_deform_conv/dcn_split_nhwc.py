@@ -19,7 +19,7 @@ import torch
 import torch.nn.functional as F
 
 from .modulated_deform_conv import (_load_ext, _ones_pad, _tap_major_weight, dcn_forward_into,
-                                    offset_conv)
+                                    offset_conv, tensor_cache_key)
 
 
 def out_size(H, pad, dil, k, stride):
@@ -48,12 +48,12 @@ def gather_cols_nhwc(x_nhwc, offset, mask=None, kH=3, kW=3, stride=1, padding=1,
 def _fold_bn(weight, bias, bn_scale, bn_shift):
     """relu(scale*(conv(x, w) + b) + shift) == relu(conv(x, w*scale) + (shift + scale*b))
     (the epilogue folding of dcn_split_nhwc.py:185-199).  Cached on the weight
-    tensor, keyed by the version counters of all four inputs (FrozenBN
-    buffers and inference weights do not change between calls; the
-    reference folds on every call)."""
+    tensor, keyed by the version counters and storage addresses of all four
+    inputs (FrozenBN buffers and inference weights do not change between
+    calls; the reference folds on every call)."""
     srcs = (bias, bn_scale, bn_shift)
-    key = (weight._version, weight.dtype, weight.device,
-           tuple(None if t is None else t._version for t in srcs))
+    key = (tensor_cache_key(weight),
+           tuple(None if t is None else tensor_cache_key(t) for t in srcs))
     cached = getattr(weight, "_bevk_bn_fold", None)
     if (cached is not None and cached[0] == key
             and all(a is b for a, b in zip(cached[1], srcs))):
@@ -229,8 +229,17 @@ def dcn_split_nhwc(x_nhwc, w_off, b_off, weight, bias=None, stride=1, padding=1,
                                       dilation, bn_scale, bn_shift, act_relu)
 
 
-def _as_int(v):
-    return v[0] if isinstance(v, (tuple, list)) else v
+def _as_int(v, what):
+    """One value for both axes.  The reference keeps the first component of a
+    pair (dcn_split_nhwc.py:306-307), which silently computes a different
+    convolution when the two differ; this build refuses such a pair."""
+    if isinstance(v, (tuple, list)):
+        if len(v) != 2 or v[0] != v[1]:
+            raise ValueError(f"dcn_apply_nchw: {what}={tuple(v)} differs between the axes; the "
+                             "NHWC path takes one value for both (use "
+                             "modulated_deform_conv2d for asymmetric geometry)")
+        return v[0]
+    return v
 
 
 def dcn_apply_nchw(x_nchw, w_off, b_off, weight, bias=None, stride=1, padding=1, dilation=1,
@@ -241,7 +250,8 @@ def dcn_apply_nchw(x_nchw, w_off, b_off, weight, bias=None, stride=1, padding=1,
     returned channels_last; a contiguous NCHW input is copied to NHWC first and
     the output returned contiguous, matching the reference.
     """
-    s, p, d = _as_int(stride), _as_int(padding), _as_int(dilation)
+    s, p, d = _as_int(stride, "stride"), _as_int(padding, "padding"), _as_int(dilation,
+                                                                               "dilation")
     is_cl = x_nchw.is_contiguous(memory_format=torch.channels_last)
     x_nhwc = x_nchw.permute(0, 2, 3, 1)
     if not is_cl:

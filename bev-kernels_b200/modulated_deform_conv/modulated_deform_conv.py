@@ -135,15 +135,47 @@ def ext_modulated_deformable_col2im_coord_opt(*args):
 # Packed weights
 # ---------------------------------------------------------------------------
 
+# Attributes under which derived copies of a weight are cached on the tensor.
+_CACHE_ATTRS = ("_bevk_packed", "_bevk_offset_gemm", "_bevk_tap_major", "_bevk_bn_fold")
+
+
+def tensor_cache_key(t: torch.Tensor):
+    """What a cached copy derived from ``t`` depends on: the version counter
+    (in-place updates through autograd-visible ops, e.g. optimizer steps), the
+    storage address (``p.data = new_tensor`` swaps, as EMA hooks and some
+    checkpoint loaders do, keep the old version counter), dtype, device and
+    shape."""
+    return (t._version, t.data_ptr(), t.dtype, t.device, tuple(t.shape))
+
+
+def invalidate_weight_caches(obj) -> None:
+    """Drop the derived copies (packed weight, tap-major weight, offset-conv
+    GEMM operand, FrozenBN fold) cached on a tensor, or on every parameter
+    and buffer of a module.  Needed only after a write the cache key cannot
+    see: ``p.data.copy_(t)`` changes neither the version counter nor the
+    storage address."""
+    tensors = ([obj] if isinstance(obj, torch.Tensor)
+               else list(obj.parameters()) + list(obj.buffers()))
+    for t in tensors:
+        for a in _CACHE_ATTRS:
+            if hasattr(t, a):
+                try:
+                    delattr(t, a)
+                except (AttributeError, RuntimeError):
+                    pass
+
+
 def packed_weight(weight: torch.Tensor, groups: int = 1) -> torch.Tensor:
     """[Cout, Cin/groups, kH, kW] -> the kernels' [Cout][kH*kW][Cin_g_pad] layout.
 
-    Cached on the weight tensor and keyed by its version counter, so a module's
-    parameter is packed once per optimizer update instead of once per call
-    (the reference permutes and copies the weight on every call,
-    dcn_split_nhwc.py:176).
+    Cached on the weight tensor and keyed by its version counter and storage
+    address (tensor_cache_key), so a module's parameter is packed once per
+    optimizer update instead of once per call (the reference permutes and
+    copies the weight on every call, dcn_split_nhwc.py:176).  An update that
+    neither bumps the version nor moves the storage -- ``p.data.copy_(t)`` --
+    is invisible to the key: call ``invalidate_weight_caches`` after it.
     """
-    key = (weight._version, weight.dtype, int(groups), weight.device, tuple(weight.shape))
+    key = (tensor_cache_key(weight), int(groups))
     cached = getattr(weight, "_bevk_packed", None)
     if cached is not None and cached[0] == key:
         return cached[1]
@@ -189,7 +221,7 @@ def offset_conv_partials(x_nhwc, w_off):
 def _offset_gemm_weight(w_off, dtype):
     """w_off [3T, Cin, kH, kW] as the GEMM operand [ld, Cin] (row t*3T + c,
     zero rows up to ld), cached on w_off like packed_weight."""
-    key = (w_off._version, dtype, w_off.device, tuple(w_off.shape))
+    key = (tensor_cache_key(w_off), dtype)
     cached = getattr(w_off, "_bevk_offset_gemm", None)
     if cached is not None and cached[0] == key:
         return cached[1]
@@ -278,7 +310,7 @@ class ModulatedDeformConv2dFunction(Function):
 def _tap_major_weight(weight, dtype):
     """weight [Cout, Cg, kH, kW] as [Cout, kH*kW*Cg] (k = t*Cg + c) in dtype,
     cached on the weight like packed_weight (the backward's dCol GEMM operand)."""
-    key = (weight._version, dtype, weight.device, tuple(weight.shape))
+    key = (tensor_cache_key(weight), dtype)
     cached = getattr(weight, "_bevk_tap_major", None)
     if cached is not None and cached[0] == key:
         return cached[1]
@@ -477,10 +509,13 @@ class ModulatedDeformConv2dPack(ModulatedDeformConv2d):
     The reference selects among 'fuse_c', 'cuda' and 'tilelang' backends; this
     build has exactly one, so ``backend=`` and ``DCN_BACKEND`` are accepted and
     recorded but do not change the computation.  groups == 1 and
-    deform_groups == 1 run the NHWC fused path (offset conv, then the fused
-    kernel reading the raw offset-conv output with the mask sigmoid applied on
-    load); other geometries compute offsets/masks explicitly and call
-    ``modulated_deform_conv2d``, as the reference does (:588-626).
+    deform_groups == 1 with the same stride, padding and dilation on both
+    axes run the NHWC fused path (offset conv, then the fused kernel reading
+    the raw offset-conv output with the mask sigmoid applied on load); other
+    geometries compute offsets/masks explicitly and call
+    ``modulated_deform_conv2d``, as the reference does (:588-626).  (The
+    reference sends asymmetric strides down its NHWC path too, which then
+    silently uses the first component for both axes.)
     """
 
     _version = 2
@@ -505,7 +540,13 @@ class ModulatedDeformConv2dPack(ModulatedDeformConv2d):
             self.conv_offset.bias.data.zero_()
 
     def forward(self, x):
-        if self.groups == 1 and self.deform_groups == 1:
+        # The NHWC path takes one stride / padding / dilation for both axes
+        # (as the reference's, dcn_split_nhwc.py:306-307, which keeps only the
+        # first component); asymmetric ones take the general path below, which
+        # honours both components.
+        square = (self.stride[0] == self.stride[1] and self.padding[0] == self.padding[1]
+                  and self.dilation[0] == self.dilation[1])
+        if self.groups == 1 and self.deform_groups == 1 and square:
             from .dcn_split_nhwc import dcn_apply_nchw
             return dcn_apply_nchw(x, self.conv_offset.weight, self.conv_offset.bias,
                                   self.weight, self.bias, self.stride, self.padding,

@@ -110,3 +110,63 @@ def test_sharding_blocks_cover_exactly():
             assert max(sizes) - min(sizes) <= 1
     with pytest.raises(ValueError):
         shard_range(4, 2, 2)
+
+
+class _FakePackExt:
+    """Stands in for the extension's packing op on the CPU: counts the calls
+    and returns a copy, so a test sees when the cache is (not) used."""
+
+    def __init__(self):
+        self.calls = 0
+
+    def dcn_pack_weight(self, w, groups):
+        self.calls += 1
+        return w.clone()
+
+
+def test_weight_caches_follow_data_swaps(monkeypatch):
+    """The derived-weight caches see `p.data = t` (new storage, old version
+    counter) and optimizer-style in-place updates; `p.data.copy_(t)` is
+    invisible to them until invalidate_weight_caches."""
+    from modulated_deform_conv import modulated_deform_conv as impl
+    fake = _FakePackExt()
+    monkeypatch.setattr(impl, "_load_ext", lambda: fake)
+    p = torch.nn.Parameter(torch.randn(8, 4, 3, 3))
+    a = impl.packed_weight(p)
+    assert impl.packed_weight(p) is a and fake.calls == 1          # cached
+    new = torch.randn(8, 4, 3, 3)
+    p.data = new                                                   # EMA / loader swap
+    b = impl.packed_weight(p)
+    assert fake.calls == 2 and torch.equal(b, new)
+    before = new.clone()
+    with torch.no_grad():
+        p.mul_(2.0)                                                # optimizer-style update
+    c = impl.packed_weight(p)
+    assert fake.calls == 3 and torch.equal(c, 2.0 * before)
+    p.data.copy_(torch.zeros(8, 4, 3, 3))                          # not visible to the key
+    assert impl.packed_weight(p) is c
+    impl.invalidate_weight_caches(p)
+    assert torch.equal(impl.packed_weight(p), torch.zeros(8, 4, 3, 3)) and fake.calls == 4
+
+
+def test_tap_major_and_bn_fold_caches_follow_data_swaps():
+    from modulated_deform_conv import modulated_deform_conv as impl
+    from modulated_deform_conv.dcn_split_nhwc import _fold_bn
+    w = torch.nn.Parameter(torch.randn(6, 4, 3, 3))
+    t1 = impl._tap_major_weight(w, torch.float32)
+    w.data = torch.randn(6, 4, 3, 3)
+    t2 = impl._tap_major_weight(w, torch.float32)
+    assert torch.equal(t2, w.detach().permute(0, 2, 3, 1).reshape(6, 36))
+    assert not torch.equal(t1, t2)
+    scale, shift = torch.rand(6) + 0.5, torch.randn(6)
+    w1, _ = _fold_bn(w, None, scale, shift)
+    scale.data = torch.rand(6) + 2.0                                  # swapped BN buffer
+    w2, _ = _fold_bn(w, None, scale, shift)
+    assert torch.allclose(w2, w.detach() * scale.view(-1, 1, 1, 1))
+    assert not torch.equal(w1, w2)
+    # module-wide invalidation clears every cached copy on its tensors
+    m = impl.ModulatedDeformConv2d(4, 6, 3, padding=1)
+    impl._tap_major_weight(m.weight, torch.float32)
+    assert hasattr(m.weight, "_bevk_tap_major")
+    impl.invalidate_weight_caches(m)
+    assert not hasattr(m.weight, "_bevk_tap_major")
