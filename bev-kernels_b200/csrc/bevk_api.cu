@@ -130,6 +130,10 @@ int64_t max_offset(const int64_t sizes[4], const int64_t strides[4]) {
   return o;
 }
 
+}  // namespace
+
+namespace bevk {
+
 int validate_dcn_tensors(const bevk_dcn_problem *p, const DcnDims &d) {
   const int T = d.T;
   const int64_t xsz[4] = {d.B, d.Cin, d.H, d.W};
@@ -142,7 +146,12 @@ int validate_dcn_tensors(const bevk_dcn_problem *p, const DcnDims &d) {
   return BEVK_OK;
 }
 
-}  // namespace
+bool input_needs_transpose(const bevk_dcn_problem *p) {
+  const int64_t *s = p->input_strides;
+  return !(s[1] == 1 && s[0] % 8 == 0 && s[2] % 8 == 0 && s[3] % 8 == 0);
+}
+
+}  // namespace bevk
 
 extern "C" {
 
@@ -195,13 +204,6 @@ BEVK_API int bevk_dcn_pack_weight(const bevk_dcn_problem *p, const void *weight,
   if (!weight || !packed_weight) return fail(BEVK_ERR_INVALID_ARGUMENT, "pack_weight: null pointer");
   return launch_dcn_pack_weight(d, weight, packed_weight, p->dtype,
                                 reinterpret_cast<cudaStream_t>(stream));
-}
-
-// The tensor-core path needs channel-contiguous input; NCHW input is first
-// transposed into the workspace.
-static bool input_needs_transpose(const bevk_dcn_problem *p) {
-  const int64_t *s = p->input_strides;
-  return !(s[1] == 1 && s[0] % 8 == 0 && s[2] % 8 == 0 && s[3] % 8 == 0);
 }
 
 BEVK_API size_t bevk_dcn_forward_workspace_bytes(const bevk_dcn_problem *p) {

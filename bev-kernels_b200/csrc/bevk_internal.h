@@ -82,6 +82,12 @@ struct DcnDims {
   int64_t M;  // B*Ho*Wo
 };
 int dcn_dims(const bevk_dcn_problem *p, DcnDims *d);
+// Checks the problem's tensor strides (no negative strides) -- shared by the
+// DCN forward entry points so they accept exactly the same problems.
+int validate_dcn_tensors(const bevk_dcn_problem *p, const DcnDims &d);
+// The tensor-core path needs channel-contiguous input with pixel rows of a
+// multiple of 8 elements; other input is first transposed to NHWC.
+bool input_needs_transpose(const bevk_dcn_problem *p);
 
 // Kernel launchers (return BEVK_OK or a status; arguments are pre-validated).
 int launch_dcn_col2im(const bevk_dcn_col2im_args *a, const DcnDims &d, const void *input,

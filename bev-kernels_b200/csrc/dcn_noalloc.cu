@@ -6,8 +6,9 @@
 // packed weight and, for NCHW input on the tensor-core path, the NHWC copy of
 // the input -- lives here in one file-scope device array instead.  Host code
 // never uses the array's name as an address: the device address is looked up
-// with cudaGetSymbolAddress once per device (with that device current) and
-// passed to the kernels.  Nothing in the array needs to start at zero: the
+// with cudaGetSymbolAddress by the first call on each device (with that device
+// current; a failed lookup is retried by the next call) and passed to the
+// kernels.  Nothing in the array needs to start at zero: the
 // packing kernel writes every packed element including the zero padding, and
 // the transpose writes every element of the input copy.
 #include <cuda_runtime.h>
@@ -26,25 +27,39 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 
-struct ScratchSlot {
-  std::once_flag once;
-  void *ptr = nullptr;
-  cudaError_t err = cudaSuccess;
-};
-ScratchSlot g_scratch_slots[kMaxDevices];
+// Device address of the scratch array per device, filled by the first
+// successful lookup (a failed lookup is not remembered: the next call retries).
+std::mutex g_scratch_mutex;
+void *g_scratch_ptr[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device (looked up once).
-int scratch_address(void **out) {
+// Device address of the scratch array on the current device.
+int scratch_address(cudaStream_t stream, void **out) {
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return fail(BEVK_ERR_CUDA, "dcn noalloc: no current device");
-  ScratchSlot &slot = g_scratch_slots[dev];
-  std::call_once(slot.once, [&slot] {
-    slot.err = cudaGetSymbolAddress(&slot.ptr, g_dcn_noalloc_scratch);
-  });
-  if (slot.err != cudaSuccess || slot.ptr == nullptr)
-    return fail(BEVK_ERR_CUDA, "dcn noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-                cudaGetErrorString(slot.err));
-  *out = slot.ptr;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    // The lookup may load the library's device code on this device, which a
+    // stream capture does not allow: refuse instead of breaking the capture.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+      (void)cudaGetLastError();
+      cap = cudaStreamCaptureStatusNone;
+    }
+    if (cap != cudaStreamCaptureStatusNone)
+      return fail(BEVK_ERR_CUDA,
+                  "dcn noalloc: the first call on device %d ran during a stream capture; make "
+                  "one call on this device before capturing",
+                  dev);
+    void *ptr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_dcn_noalloc_scratch);
+    if (err != cudaSuccess || ptr == nullptr) {
+      (void)cudaGetLastError();  // leave no error pending for later checks in this thread
+      return fail(BEVK_ERR_CUDA, "dcn noalloc: cudaGetSymbolAddress failed on device %d: %s",
+                  dev, cudaGetErrorString(err));
+    }
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
   return BEVK_OK;
 }
 
@@ -65,17 +80,14 @@ extern "C" BEVK_API int bevk_dcn_forward_noalloc(const bevk_dcn_problem *p, cons
   if (st != BEVK_OK) return st;
   if (!input || !offset || !mask || !weight || !output || (p->has_bias && !bias))
     return fail(BEVK_ERR_INVALID_ARGUMENT, "dcn_forward_noalloc: null pointer");
-  for (int i = 0; i < 4; ++i)
-    if (p->input_strides[i] < 0 || p->offset_strides[i] < 0 || p->mask_strides[i] < 0 ||
-        p->output_strides[i] < 0)
-      return fail(BEVK_ERR_INVALID_ARGUMENT, "dcn_forward_noalloc: negative strides are not supported");
+  // the same checks and path choice as bevk_dcn_forward
+  st = validate_dcn_tensors(p, d);
+  if (st != BEVK_OK) return st;
 
   const size_t esz = dtype_size(p->dtype);
   const int64_t *xs_in = p->input_strides;
-  const bool channel_contig = xs_in[1] == 1 && xs_in[0] % 8 == 0 && xs_in[2] % 8 == 0 &&
-                              xs_in[3] % 8 == 0;
-  const bool tc = dcn_tc_supported(p, d) && (!channel_contig || aligned(input, 16));
-  const bool transpose = tc && !channel_contig;
+  const bool tc = dcn_tc_supported(p, d) && (input_needs_transpose(p) || aligned(input, 16));
+  const bool transpose = tc && input_needs_transpose(p);
   const size_t wbytes = static_cast<size_t>(d.Cout) * d.T * d.Cin_g_pad * esz;
   const size_t xbytes = transpose ? static_cast<size_t>(d.B) * d.H * d.W * d.Cin * esz : 0;
   const size_t need = round256(wbytes) + xbytes;
@@ -87,10 +99,10 @@ extern "C" BEVK_API int bevk_dcn_forward_noalloc(const bevk_dcn_problem *p, cons
                 need, wbytes, transpose ? " + NHWC input copy" : "",
                 static_cast<size_t>(BEVK_DCN_NOALLOC_SCRATCH_BYTES));
 
-  void *scratch = nullptr;
-  st = scratch_address(&scratch);
-  if (st != BEVK_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  void *scratch = nullptr;
+  st = scratch_address(s, &scratch);
+  if (st != BEVK_OK) return st;
   unsigned char *base = static_cast<unsigned char *>(scratch);
   void *wpk = base;
   st = launch_dcn_pack_weight(d, weight, wpk, p->dtype, s);

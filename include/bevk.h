@@ -217,7 +217,8 @@ BEVK_API int bevk_dcn_forward_zoff(const bevk_dcn_problem *p, const bevk_dcn_zof
  *
  * The first call on a device looks up the array's device address (once per
  * device, with that device current); make that first call before capturing
- * a stream into a CUDA graph.  All calls on a device share the one array and
+ * a stream into a CUDA graph -- a first call made during a capture returns
+ * BEVK_ERR_CUDA without touching the stream.  All calls on a device share the one array and
  * its contents persist between calls (nothing in it needs to start at zero):
  * calls whose kernels can overlap on the GPU -- different streams without
  * ordering between them -- race on it, so serialise them.

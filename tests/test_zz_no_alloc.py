@@ -61,22 +61,26 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda, case):
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
-    # NCHW fp16 input of 8 x 512 x 64 x 64 needs a 32 MiB NHWC copy + 4.5 MiB of packed
-    # weight -> beyond the 32 MiB built-in scratch.
+    # a 2048 -> 2048 channel 3x3 fp16 layer: its packed weight alone
+    # (2048 * 9 * 2048 * 2 bytes = 72 MiB) exceeds the 32 MiB built-in scratch,
+    # so the call refuses on every path (tensor-core or SIMT, NCHW or NHWC)
+    # before it touches any pointer.
+    B, C, H, W = 1, 2048, 8, 8
     p = cabi.DcnProblem()
     p.dtype = cabi.DTYPE_F16
-    p.batch, p.in_channels, p.height, p.width = 8, 512, 64, 64
-    p.out_channels, p.kernel_h, p.kernel_w = 512, 3, 3
+    p.batch, p.in_channels, p.height, p.width = B, C, H, W
+    p.out_channels, p.kernel_h, p.kernel_w = C, 3, 3
     p.stride_h = p.stride_w = p.pad_h = p.pad_w = p.dilation_h = p.dilation_w = 1
     p.groups = p.deformable_groups = 1
-    hw = 64 * 64
-    for i, v in enumerate((512 * hw, hw, 64, 1)):
+    hw = H * W
+    for i, v in enumerate((C * hw, hw, W, 1)):
         p.input_strides[i] = v
         p.output_strides[i] = v
-    for i, v in enumerate((18 * hw, hw, 64, 1)):
+    for i, v in enumerate((18 * hw, hw, W, 1)):
         p.offset_strides[i] = v
-    for i, v in enumerate((9 * hw, hw, 64, 1)):
+    for i, v in enumerate((9 * hw, hw, W, 1)):
         p.mask_strides[i] = v
+    assert cabi.lib().bevk_dcn_packed_weight_bytes(ctypes.byref(p)) > (32 << 20)
     fake = 256  # never dereferenced: the size check comes first
     st = cabi.lib().bevk_dcn_forward_noalloc(ctypes.byref(p), fake, fake, fake, fake, None, fake,
                                              None)
