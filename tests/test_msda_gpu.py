@@ -67,6 +67,31 @@ def test_small_cases(cuda, cfg, dt):
         assert out.dtype == dt and rel_l2(out, want) <= HALF_REL
 
 
+# Larger multi-level cases (150k+ units: batch x queries x heads) with partial
+# load batches (L*P = 9), two rounds of samples (L*P = 48) and large levels.
+LARGE = [
+    dict(B=2, shapes=[(40, 60), (20, 30), (10, 15), (5, 8)], M=8, C=32, Q=10000, P=8),
+    dict(B=1, shapes=[(30, 50), (15, 25), (8, 13)], M=8, C=32, Q=19000, P=3),
+    dict(B=3, shapes=[(16, 20), (8, 10), (4, 5), (2, 3)], M=4, C=32, Q=13000, P=12),
+    dict(B=1, shapes=[(120, 160), (60, 80)], M=8, C=32, Q=19500, P=4),
+]
+
+
+@pytest.mark.parametrize("cfg", LARGE, ids=[f"l{i}" for i in range(len(LARGE))])
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16],
+                         ids=["f32", "f16", "bf16"])
+def test_large_multilevel_cases(cuda, cfg, dt):
+    value, shapes, lsi, loc, attn = msda_inputs(11, oob_frac=0.05, **cfg)
+    value, loc, attn = (t.to(cuda, dt) for t in (value, loc, attn))
+    shapes, lsi = shapes.to(cuda), lsi.to(cuda)
+    want = _oracle(value, shapes, lsi, loc, attn)
+    out = cabi_msda_forward(value, shapes, lsi, loc, attn)
+    if dt == torch.float32:
+        assert rel_l2(out, want) <= FP32_REL and max_abs(out, want) <= FP32_ABS
+    else:
+        assert out.dtype == dt and rel_l2(out, want) <= HALF_REL
+
+
 @pytest.mark.parametrize("name", ["cfg4", "cfg5"])
 def test_baseline_configs_full_size(cuda, name):
     import ms_deform_attn
