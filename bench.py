@@ -21,12 +21,16 @@ event reasons are sampled through NVML during the timed region.
 Also reported on the same line: ``e2e`` (the same metric through the public
 ``modulated_deform_conv2d`` call with inputs copied from pinned host memory and
 the output copied back every step), the roofline of the fused kernel against
-MEASURED_PEAKS.json, the CPU oracle timed on a bounded sample (rank 0, N = 1)
-and, in ``secondary``, BASELINE configs 3 (DCN bf16), 4 and 5 (MSDA fp32), the
-Pack forward, the DCN and MSDA backward, and the 5-chain (48 images, each a
-cfg5 MSDA camera slice and a cfg3 DCN image, in contiguous blocks per rank:
-strong scaling over the ranks, per-image checksums all-gathered and checked
-on rank 0 outside the timed region).
+MEASURED_PEAKS.json, the CPU oracle timed on a bounded sample (rank 0, N = 1),
+``legs`` (the Pack forward, the DCN and MSDA backward, the 5-chain: 48 images,
+each a cfg5 MSDA camera slice and a cfg3 DCN image, in contiguous blocks per
+rank, strong scaling, per-image checksums all-gathered and checked on rank 0
+outside the timed region) and, last, ``configs``: for each BASELINE config
+(1-5) the device us/call, its roofline fraction (tensor peak for DCN, HBM for
+MSDA), the end-to-end us/step through the public call with pinned host
+buffers, the CPU oracle's us/call on all host threads, and for MSDA the
+fp16/bf16 variants.  A spin kernel queued ahead of each start event keeps the
+host's submission latency out of the timed region.
 
 ``--impl reference`` times the reference algorithm on the host cores instead
 (the CPU oracle restatement in oracle/, all threads) on the same workload and
@@ -54,6 +58,9 @@ L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 DCN_CFGS = {
+    "cfg1": dict(B=1, C=64, H=32, W=32, Cout=64, dtype="float32", big=0.0, off_std=1.0,
+                 bias=True, layout="nchw",
+                 desc="DCNv2 plumbing fwd: 1x64->64, 32x32, 3x3 s1 p1, bias, NCHW fp32"),
     "cfg2": dict(B=6, C=512, H=29, W=50, Cout=512, dtype="float16", big=0.0,
                  desc="DCNv2 stage-4 conv2 fwd: 6x512->512, 29x50, 3x3 s1 p1, NHWC fp16"),
     "cfg3": dict(B=6, C=256, H=58, W=100, Cout=256, dtype="bfloat16", big=0.05,
@@ -94,22 +101,40 @@ def _out(n, pad, dil, k, stride):
     return (n + 2 * pad - (dil * (k - 1) + 1)) // stride + 1
 
 
+_ESZ = {"float32": 4, "float16": 2, "bfloat16": 2}
+
+
 def dcn_work(cfg):
     """Algorithmic FLOPs and unique bytes of one DCN forward: 2*M*N*K FLOPs; input,
-    offset, mask, weight and output each read or written once."""
+    offset, mask, weight, bias and output each read or written once."""
     B, C, H, W, Co = cfg["B"], cfg["C"], cfg["H"], cfg["W"], cfg["Cout"]
     Ho, Wo = _out(H, 1, 1, 3, 1), _out(W, 1, 1, 3, 1)
     flops = 2.0 * B * Ho * Wo * Co * C * 9
-    e = 2  # fp16 / bf16
-    nbytes = e * (B * C * H * W + Co * C * 9 + B * 18 * Ho * Wo + B * 9 * Ho * Wo + B * Co * Ho * Wo)
+    e = _ESZ[cfg["dtype"]]
+    nbytes = e * (B * C * H * W + Co * C * 9 + B * 18 * Ho * Wo + B * 9 * Ho * Wo +
+                  B * Co * Ho * Wo + (Co if cfg.get("bias") else 0))
     return flops, nbytes
 
 
-def msda_bytes(cfg):
+def msda_bytes(cfg, esz=4):
     B, M, C, Q, P = cfg["B"], cfg["M"], cfg["C"], cfg["Q"], cfg["P"]
     L = len(cfg["shapes"])
     S = sum(h * w for h, w in cfg["shapes"])
-    return 4 * (B * S * M * C + B * Q * M * L * P * 2 + B * Q * M * L * P + B * Q * M * C)
+    return esz * (B * S * M * C + B * Q * M * L * P * 2 + B * Q * M * L * P + B * Q * M * C)
+
+
+def cpu_info():
+    """Host CPU model and logical core count (for the CPU baselines)."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"model": model, "logical_cores": os.cpu_count()}
 
 
 class ClockSampler:
@@ -196,7 +221,7 @@ def dcn_sets(cfg, n_sets, seed, img0, device):
         for b in range(B):
             g.manual_seed(image_seed(seed, img0 + b, s))
             xs.append(torch.randn(1, C, H, W, generator=g, device=device))
-            off = torch.randn(1, 18, H, W, generator=g, device=device) * 2.0
+            off = torch.randn(1, 18, H, W, generator=g, device=device) * cfg.get("off_std", 2.0)
             if cfg["big"]:
                 sel = torch.rand(off.shape, generator=g, device=device) < cfg["big"]
                 sign = torch.where(torch.rand(off.shape, generator=g, device=device) < 0.5,
@@ -206,14 +231,20 @@ def dcn_sets(cfg, n_sets, seed, img0, device):
             masks.append(torch.sigmoid(torch.randn(1, 9, H, W, generator=g, device=device)))
         g.manual_seed(seed * 7919 + s)
         w = torch.randn(Co, C, 3, 3, generator=g, device=device) * math.sqrt(2.0 / (C * 9))
-        x = torch.cat(xs).to(dt).contiguous(memory_format=torch.channels_last)
-        out = torch.empty(B, Co, H, W, dtype=dt, device=device, memory_format=torch.channels_last)
+        bias = (torch.randn(Co, generator=g, device=device).to(dt) if cfg.get("bias")
+                else None)
+        fmt = (torch.contiguous_format if cfg.get("layout") == "nchw"
+               else torch.channels_last)
+        x = torch.cat(xs).to(dt).contiguous(memory_format=fmt)
+        out = torch.empty(B, Co, H, W, dtype=dt, device=device, memory_format=fmt)
         sets.append(dict(x=x, off=torch.cat(offs).to(dt), mask=torch.cat(masks).to(dt),
-                         w=w.to(dt), out=out))
+                         w=w.to(dt), b=bias, out=out))
     return sets
 
 
-def msda_sets(cfg, n_sets, seed, device):
+def msda_sets(cfg, n_sets, seed, device, dtype=None):
+    """n_sets independent MSDA input sets (value, locations, attention weights
+    generated in fp32, then cast to ``dtype`` when given)."""
     import torch
     sets = []
     B, M, C, Q, P = cfg["B"], cfg["M"], cfg["C"], cfg["Q"], cfg["P"]
@@ -232,6 +263,8 @@ def msda_sets(cfg, n_sets, seed, device):
             sel = torch.rand(B, Q, M, L, P, 1, generator=g, device=device) < cfg["oob"]
             loc = torch.where(sel, loc * 1.4 - 0.2, loc)
         attn = torch.softmax(torch.randn(B, Q, M, L * P, generator=g, device=device), -1)
+        if dtype is not None:
+            value, loc, attn = value.to(dtype), loc.to(dtype), attn.to(dtype)
         sets.append(dict(value=value, loc=loc, attn=attn.view(B, Q, M, L, P),
                          shapes=torch.tensor(shapes, dtype=torch.int64, device=device),
                          lsi=torch.tensor(lsi, dtype=torch.int64, device=device)))
@@ -388,6 +421,7 @@ def graph_time(step_fns, steps, warmup, stream, clocks=None, dist=None):
     ctx = clocks if clocks is not None else _Null()
     with ctx:
         with torch.cuda.stream(stream):
+            _cover_launch_gap(stream)
             start.record(stream)
             for g in graphs:
                 g.replay()
@@ -398,6 +432,16 @@ def graph_time(step_fns, steps, warmup, stream, clocks=None, dist=None):
     ms = start.elapsed_time(end)
     del graphs
     return _max_over_ranks(ms, dist)
+
+
+def _cover_launch_gap(stream):
+    """Queue a ~2 ms spin kernel ahead of the start event, so the GPU is busy
+    while the host submits the timed graphs / copies: the events then bracket
+    only the device's work on the K steps, not the host's submission latency
+    (which otherwise adds its own length / K to every step of a short run)."""
+    import torch
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(4_000_000)
 
 
 class _Null:
@@ -431,7 +475,7 @@ def bench_dcn(cfg_name, steps, warmup, device, seed, img0, stream, dist=None, cl
         s["wpk"] = mdc.packed_weight(s["w"])
 
     def make(s):
-        return lambda: ext.dcn_forward(s["x"], s["off"], s["mask"], s["wpk"], None, s["out"],
+        return lambda: ext.dcn_forward(s["x"], s["off"], s["mask"], s["wpk"], s["b"], s["out"],
                                        3, 3, 1, 1, 1, 1, 1, 1, 1, 1, False)
 
     ms = graph_time([make(s) for s in sets], steps, warmup, stream, clocks, dist)
@@ -505,27 +549,25 @@ def bench_dcn_bwd(cfg_name, steps, warmup, device, seed, stream):
     return dict(ms=ms, flops=2 * flops, per_launch_s=ms / 1e3 / steps, n_sets=len(sets))
 
 
-def bench_dcn_e2e(cfg_name, steps, warmup, device, sets, stream, clocks=None, dist=None):
-    """Public-API end-to-end: every step copies its inputs from pinned host memory
-    to the device, runs modulated_deform_conv2d and reads its output back into
-    pinned host memory.  The steps are pipelined the way an inference loop runs
-    them: the host->device copy of step k+1 and the device->host copy of step
-    k-1 run on their own streams while step k computes (two buffer sets,
-    ordered by events), so the per-step time is that of the slowest of the
-    three, not their sum."""
+def e2e_time(host_in, run, steps, warmup, stream, clocks=None, dist=None):
+    """Public-API end-to-end time of `steps` steps: every step copies its inputs
+    (``host_in``, pinned host tensors) to the device, runs ``run(dev_inputs)``
+    (the public call; it allocates and returns its output) and reads the output
+    back into pinned host memory.  The steps are pipelined the way an
+    inference loop runs them: the host->device copy of step k+1 and the
+    device->host copy of step k-1 run on their own streams while step k
+    computes (two buffer sets, ordered by events), so the per-step time is
+    that of the slowest of the three, not their sum.
+    Returns (ms max over ranks, h2d bytes per step, d2h bytes per step)."""
     import torch
-    import modulated_deform_conv as mdc
-    cfg = DCN_CFGS[cfg_name]
-    s0 = sets[0]
-    hx = s0["x"].cpu().pin_memory()                   # keeps channels_last strides
-    ho = s0["off"].cpu().pin_memory()
-    hm = s0["mask"].cpu().pin_memory()
-    w = s0["w"]
-    B, Co, H, W = cfg["B"], cfg["Cout"], cfg["H"], cfg["W"]
-    dev_in = [(torch.empty_like(s0["x"]), torch.empty_like(s0["off"]),
-               torch.empty_like(s0["mask"])) for _ in range(2)]
-    hout = [torch.empty(B, Co, H, W, dtype=s0["x"].dtype).pin_memory() for _ in range(2)]
-    h2d = sum(t.numel() * t.element_size() for t in (hx, ho, hm))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    dev_in = [[torch.empty_like(h, device=dev) for h in host_in] for _ in range(2)]
+    with torch.cuda.stream(stream):
+        probe = run(dev_in[0])
+    torch.cuda.synchronize()
+    hout = [torch.empty(probe.shape, dtype=probe.dtype).pin_memory() for _ in range(2)]
+    del probe
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = hout[0].numel() * hout[0].element_size()
     s_in, s_comp, s_out = torch.cuda.Stream(), stream, torch.cuda.Stream()
     ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -535,17 +577,15 @@ def bench_dcn_e2e(cfg_name, steps, warmup, device, sets, stream, clocks=None, di
 
     def step(k):
         i = k % 2
-        dx, do, dm = dev_in[i]
         with torch.cuda.stream(s_in):
             s_in.wait_event(ev_comp[i])               # step k-2 has consumed buffer set i
-            dx.copy_(hx, non_blocking=True)
-            do.copy_(ho, non_blocking=True)
-            dm.copy_(hm, non_blocking=True)
+            for d, h in zip(dev_in[i], host_in):
+                d.copy_(h, non_blocking=True)
             ev_in[i].record(s_in)
         with torch.cuda.stream(s_comp):
             s_comp.wait_event(ev_in[i])
             s_comp.wait_event(ev_out[i])              # step k-2's output has been read back
-            ys[i] = mdc.modulated_deform_conv2d(dx, do, dm, w, None, 1, 1, 1)
+            ys[i] = run(dev_in[i])
             ev_comp[i].record(s_comp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_comp[i])
@@ -561,6 +601,7 @@ def bench_dcn_e2e(cfg_name, steps, warmup, device, sets, stream, clocks=None, di
     torch.cuda.synchronize()
     ctx = clocks if clocks is not None else _Null()
     with ctx:
+        _cover_launch_gap(s_in)
         start.record(s_in)
         for k in range(steps):
             step(k)
@@ -572,11 +613,37 @@ def bench_dcn_e2e(cfg_name, steps, warmup, device, sets, stream, clocks=None, di
     return ms, h2d, d2h
 
 
-def bench_msda(cfg_name, steps, warmup, device, seed, stream):
+def bench_dcn_e2e(cfg_name, steps, warmup, sets, stream, clocks=None, dist=None):
+    """DCN forward end to end through modulated_deform_conv2d (the reference
+    Function's public call) with x / offset / mask from pinned host memory."""
+    import modulated_deform_conv as mdc
+    s0 = sets[0]
+    host = [s0[k].cpu().pin_memory() for k in ("x", "off", "mask")]  # keeps x's strides
+    w, b = s0["w"], s0["b"]
+    return e2e_time(host, lambda d: mdc.modulated_deform_conv2d(d[0], d[1], d[2], w, b, 1, 1, 1),
+                    steps, warmup, stream, clocks, dist)
+
+
+def bench_msda_e2e(cfg_name, steps, warmup, device, seed, stream, dist=None):
+    """MSDA forward end to end through MultiScaleDeformableAttnFunction.apply
+    with value / locations / attention weights from pinned host memory (the
+    level shapes and start indices are per-model constants kept on the device)."""
+    import ms_deform_attn
+    s0 = msda_sets(MSDA_CFGS[cfg_name], 1, seed, device)[0]
+    host = [s0[k].cpu().pin_memory() for k in ("value", "loc", "attn")]
+    shapes, lsi = s0["shapes"], s0["lsi"]
+    del s0
+    fn = ms_deform_attn.MultiScaleDeformableAttnFunction.apply
+    return e2e_time(host, lambda d: fn(d[0], shapes, lsi, d[1], d[2], 64), steps, warmup,
+                    stream, None, dist)
+
+
+def bench_msda(cfg_name, steps, warmup, device, seed, stream, dtype=None):
+    import torch
     import _ms_deform_attn_ext as ext
     cfg = MSDA_CFGS[cfg_name]
-    nbytes = msda_bytes(cfg)
-    sets = msda_sets(cfg, n_sets_for(nbytes, lo=2, hi=4), seed, device)
+    nbytes = msda_bytes(cfg, 4 if dtype in (None, torch.float32) else 2)
+    sets = msda_sets(cfg, n_sets_for(nbytes, lo=2, hi=4), seed, device, dtype)
 
     def make(s):
         return lambda: ext.forward(s["value"], s["shapes"], s["lsi"], s["loc"], s["attn"], 64,
@@ -624,35 +691,91 @@ def bench_msda_bwd(cfg_name, steps, warmup, device, seed, stream):
 
 
 # ----------------------------------------------------------------------------- CPU legs
-def cpu_dcn_sample(cfg_name, target_s, seed):
-    """Time the CPU oracle on a bounded pixel range of the workload (all host threads).
-    Returns (TFLOP/s, pixels per call, calls, threads)."""
-    import numpy as np
+def _median_calls(fn, calls=5):
+    """Median wall time of `calls` calls of fn(i) after one warm-up call."""
+    fn(0)
+    times = []
+    for i in range(calls):
+        t0 = time.perf_counter()
+        fn(i)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times)
+
+
+def cpu_dcn(cfg_name, target_s, seed):
+    """The CPU oracle (oracle/bevk_oracle.c: the reference's DCN forward in fp32
+    math, double accumulation) on all host threads over a bounded range of
+    output pixels of the workload, median of 5 calls after a warm-up.
+    Returns dict(us per full call, TFLOP/s, pixels per call, threads)."""
     import torch
     from oracle import oracle
     cfg = DCN_CFGS[cfg_name]
     s = dcn_sets(cfg, 1, seed, 0, torch.device("cpu"))[0]
     x = s["x"].float().contiguous().numpy()
     off, mask, w = (s[k].float().contiguous().numpy() for k in ("off", "mask", "w"))
+    b = None if s["b"] is None else s["b"].float().numpy()
     B, C, H, W, Co = cfg["B"], cfg["C"], cfg["H"], cfg["W"], cfg["Cout"]
     M = B * H * W
     per_px = 2.0 * Co * C * 9
+    probe = min(M, 256)
     t0 = time.perf_counter()
-    oracle.dcn_forward(x, off, mask, w, None, 1, 1, 1, pix_range=(0, 256))
-    t_px = max((time.perf_counter() - t0) / 256, 1e-7)
-    npix = int(min(M, max(256, target_s / t_px)))
-    times = []
-    for r in range(3):
-        lo = (r * npix) % max(1, M - npix + 1)
-        t0 = time.perf_counter()
-        oracle.dcn_forward(x, off, mask, w, None, 1, 1, 1, pix_range=(lo, lo + npix))
-        times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    return per_px * npix / t / 1e12, npix, len(times), oracle.max_threads()
+    oracle.dcn_forward(x, off, mask, w, b, 1, 1, 1, pix_range=(0, probe))
+    t_px = max((time.perf_counter() - t0) / probe, 1e-8)
+    npix = int(min(M, max(probe, target_s / t_px)))
+
+    def call(i):
+        lo = (i * npix) % max(1, M - npix + 1)
+        oracle.dcn_forward(x, off, mask, w, b, 1, 1, 1, pix_range=(lo, lo + npix))
+
+    t = _median_calls(call)
+    return dict(us=t / npix * M * 1e6, tflops=per_px * npix / t / 1e12, npix=npix, M=M,
+                threads=oracle.max_threads())
 
 
-def run_reference(args):
-    """--impl reference: the reference algorithm (oracle port) on the host cores."""
+def cpu_msda(cfg_name, target_s, seed):
+    """The CPU oracle's MSDA forward (the reference kernel's math,
+    ms_deform_attn_kernels.cuh:559-623) on all host threads over a bounded range
+    of (batch, query, head) units, median of 5 calls after a warm-up.
+    Returns dict(us per full call, GB/s algorithmic, units per call, threads)."""
+    import torch
+    from oracle import oracle
+    cfg = MSDA_CFGS[cfg_name]
+    s = msda_sets(cfg, 1, seed, torch.device("cpu"))[0]
+    args = [s[k].numpy() for k in ("value", "shapes", "lsi", "loc", "attn")]
+    units = cfg["B"] * cfg["Q"] * cfg["M"]
+    probe = min(units, 4096)
+    t0 = time.perf_counter()
+    oracle.msda_forward(*args, unit_range=(0, probe))
+    t_u = max((time.perf_counter() - t0) / probe, 1e-9)
+    n = int(min(units, max(probe, target_s / t_u)))
+
+    def call(i):
+        lo = (i * n) % max(1, units - n + 1)
+        oracle.msda_forward(*args, unit_range=(lo, lo + n))
+
+    t = _median_calls(call)
+    full_s = t / n * units
+    return dict(us=full_s * 1e6, gbps=msda_bytes(cfg) / full_s / 1e9, units=n, total=units,
+                threads=oracle.max_threads())
+
+
+def headline_config(world):
+    """The headline's `config` (shared by both arms, so the driver can compare
+    them): BASELINE cfg2, weak-scaled over the ranks."""
+    cfg = DCN_CFGS["cfg2"]
+    _, nbytes = dcn_work(cfg)
+    n_sets = n_sets_for(nbytes)
+    return {"workload": cfg["desc"] + " (fp32 accumulate)", "global_batch": cfg["B"] * world,
+            "parallelism": f"dp{world} (cameras sharded across ranks, no collective on the "
+                           "data path)",
+            "l2": f"inputs rotate over {n_sets} independent sets "
+                  f"({n_sets * nbytes / 2**20:.0f} MiB > 126 MB L2)"}
+
+
+def run_reference(args, world):
+    """--impl reference: the reference algorithm (the oracle port of the DCN
+    forward) on all host threads, same metric, unit and config as our arm; a
+    step is a bounded sample of the cfg2 workload."""
     from oracle import oracle
     import torch
     cfg = DCN_CFGS["cfg2"]
@@ -676,21 +799,31 @@ def run_reference(args):
     el = time.perf_counter() - t0
     value = per_px * npix * args.steps / el / 1e12
     threads = oracle.max_threads()
+    cpu = cpu_info()
     sample = (f"{npix} of {M} output pixels of cfg2 per step (C oracle, fp32 math, "
-              f"double accumulation, {threads} OpenMP threads)")
+              f"double accumulation, {threads} OpenMP threads on {cpu['model']})")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE cfg2 "
-        "distributions)",
-        "config": {"workload": cfg["desc"], "sample": sample},
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE cfg2 "
+        "shapes and distributions)",
+        "config": headline_config(world),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def _r(v, nd=3):
+    """Round to `nd` significant digits for the compact per-config record."""
+    if v is None:
+        return None
+    if v == 0:
+        return 0.0
+    return float(f"{v:.{nd}g}")
 
 
 # ----------------------------------------------------------------------------- main
@@ -702,9 +835,10 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--only", choices=("cfg2", "cfg3", "cfg4", "cfg5", "bwd_cfg2", "bwd_cfg3",
-                                       "bwd_cfg4", "bwd_cfg5", "pack_cfg2", "pack_cfg3",
-                                       "chain"),
+    ap.add_argument("--only", choices=("cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "cfg4_f16",
+                                       "cfg5_f16", "cfg4_bf16", "cfg5_bf16", "bwd_cfg2",
+                                       "bwd_cfg3", "bwd_cfg4", "bwd_cfg5", "pack_cfg2",
+                                       "pack_cfg3", "chain"),
                     help="time one workload's kernel only (profiling runs: no e2e, "
                          "secondary or CPU legs; prints a reduced line)")
     args = ap.parse_args()
@@ -716,7 +850,7 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            run_reference(args)
+            run_reference(args, world)
         return
 
     import datetime
@@ -732,6 +866,7 @@ def main():
     stream = torch.cuda.Stream(device=device)
     peaks, peaks_src = _peaks()
     seed = 2026
+    half = {"f16": torch.float16, "bf16": torch.bfloat16}
 
     if args.only:
         if args.only == "chain":
@@ -756,7 +891,8 @@ def main():
             r = bench_msda_bwd(args.only[4:], args.steps, args.warmup, device, seed, stream)
             extra = {"algorithmic_GBps": r["bytes"] / r["per_launch_s"] / 1e9}
         else:
-            r = bench_msda(args.only, args.steps, args.warmup, device, seed, stream)
+            name, _, dt = args.only.partition("_")
+            r = bench_msda(name, args.steps, args.warmup, device, seed, stream, half.get(dt))
             extra = {"algorithmic_GBps": r["bytes"] / r["per_launch_s"] / 1e9}
         if rank == 0:
             print(json.dumps({"profile_run": True, "workload": args.only,
@@ -779,87 +915,86 @@ def main():
             "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
             "traffic": _traffic("dcn_fwd_tc cfg2"),
             "peak_source": f"{peaks_src} bf16_tflops (burst; kernel timed alone)",
-            "algorithmic_bytes": nbytes,
-            "hbm_frac": nbytes / res["per_launch_s"] / 1e9 / peaks["hbm_gbs"]}
+            "algorithmic_bytes": nbytes}
 
     e2e_clocks = ClockSampler(local_rank)
-    e2e_ms, h2d, d2h = bench_dcn_e2e(cfg_name, args.steps, args.warmup, device, res["sets"],
-                                     stream, e2e_clocks, dist)
-    e2e_value = world * flops * args.steps / (e2e_ms / 1e3) / 1e12
+    e2e_steps = min(args.steps, 200)
+    e2e_ms, h2d, d2h = bench_dcn_e2e(cfg_name, e2e_steps, args.warmup, res["sets"], stream,
+                                     e2e_clocks, dist)
+    e2e_value = world * flops * e2e_steps / (e2e_ms / 1e3) / 1e12
     del res["sets"]
     torch.cuda.empty_cache()
 
-    secondary = {}
+    # compact per-config record, printed last on the line
+    tens_peak, hbm = peaks["bf16_tflops"], peaks["hbm_gbs"]
+    configs = {"cfg2": {"us": _r(res["per_launch_s"] * 1e6),
+                        "frac": _r(achieved / tens_peak),
+                        "e2e_us": _r(e2e_ms * 1e3 / e2e_steps)}}
+    legs = {}
+    k2 = min(args.steps, 500)
+    ke = min(args.steps, 20)
     if not args.no_secondary:
-        k2 = min(args.steps, 500)
+        r1 = bench_dcn("cfg1", k2, args.warmup, device, seed + 1, 0, stream)
+        e1 = bench_dcn_e2e("cfg1", ke, args.warmup, r1["sets"], stream)
+        del r1["sets"]
+        configs["cfg1"] = {"us": _r(r1["per_launch_s"] * 1e6), "frac": None,
+                           "e2e_us": _r(e1[0] * 1e3 / ke)}
         r3 = bench_dcn("cfg3", k2, args.warmup, device, seed + 1, cfg["B"] * rank, stream)
+        e3 = bench_dcn_e2e("cfg3", ke, args.warmup, r3["sets"], stream)
         del r3["sets"]
-        a3 = r3["flops"] / r3["per_launch_s"] / 1e12
-        secondary["dcn_cfg3"] = {"workload": DCN_CFGS["cfg3"]["desc"],
-                                 "us_per_call": r3["per_launch_s"] * 1e6,
-                                 "tflops": a3, "frac_tensor_peak": a3 / peaks["bf16_tflops"],
-                                 "traffic": _traffic("dcn_fwd_tc cfg3")}
+        configs["cfg3"] = {"us": _r(r3["per_launch_s"] * 1e6),
+                           "frac": _r(r3["flops"] / r3["per_launch_s"] / 1e12 / tens_peak),
+                           "e2e_us": _r(e3[0] * 1e3 / ke)}
         torch.cuda.empty_cache()
         for name in ("cfg4", "cfg5"):
             r = bench_msda(name, k2, args.warmup, device, seed + 2, stream)
-            gbs = r["bytes"] / r["per_launch_s"] / 1e9
-            secondary[f"msda_{name}"] = {
-                "workload": MSDA_CFGS[name]["desc"], "us_per_call": r["per_launch_s"] * 1e6,
-                "algorithmic_GBps": gbs, "frac_hbm_peak": gbs / peaks["hbm_gbs"],
-                "roofline_us": r["bytes"] / (peaks["hbm_gbs"] * 1e9) * 1e6,
-                "traffic": _traffic(f"msda_fwd {name}")}
+            roof_us = r["bytes"] / (hbm * 1e9) * 1e6
+            em = bench_msda_e2e(name, ke, args.warmup, device, seed + 2, stream)
+            entry = {"us": _r(r["per_launch_s"] * 1e6),
+                     "frac": _r(roof_us / (r["per_launch_s"] * 1e6)),
+                     "e2e_us": _r(em[0] * 1e3 / ke)}
+            torch.cuda.empty_cache()
+            for tag, dt in half.items():
+                rh = bench_msda(name, k2, args.warmup, device, seed + 2, stream, dt)
+                entry[f"{tag}_us"] = _r(rh["per_launch_s"] * 1e6)
+                entry[f"{tag}_frac"] = _r(rh["bytes"] / (hbm * 1e3) / (rh["per_launch_s"] * 1e6))
+                torch.cuda.empty_cache()
+            configs[name] = entry
+        for name in ("cfg2", "cfg3"):
+            r = bench_dcn_pack(name, min(k2, 200), args.warmup, device, seed + 5, stream, True)
+            legs[f"pack{name[-1]}_us"] = _r(r["per_launch_s"] * 1e6)
             torch.cuda.empty_cache()
         for name in ("cfg2", "cfg3"):
-            for fused in (False, True):
-                r = bench_dcn_pack(name, min(k2, 200), args.warmup, device, seed + 5, stream,
-                                   fused)
-                a = r["flops"] / r["per_launch_s"] / 1e12
-                how = ("offset conv as one GEMM (fp32 out) + tap-sum kernel"
-                       if fused else "offset conv on cuDNN")
-                secondary[f"dcn_pack_{name}_{'gemm' if fused else 'cudnn'}"] = {
-                    "workload": DCN_CFGS[name]["desc"].replace(" fwd", " Pack fwd") +
-                                f" with FrozenBN+ReLU; {how}",
-                    "us_per_call": r["per_launch_s"] * 1e6, "tflops": a,
-                    "frac_tensor_peak": a / peaks["bf16_tflops"]}
-                torch.cuda.empty_cache()
-        for name in ("cfg2", "cfg3"):
             r = bench_dcn_bwd(name, min(k2, 100), args.warmup, device, seed + 4, stream)
-            a = r["flops"] / r["per_launch_s"] / 1e12
-            secondary[f"dcn_bwd_{name}"] = {
-                "workload": DCN_CFGS[name]["desc"].replace(" fwd", " bwd") +
-                            " (all five gradients)",
-                "us_per_call": r["per_launch_s"] * 1e6, "tflops": a,
-                "frac_tensor_peak": a / peaks["bf16_tflops"]}
+            legs[f"dcn_bwd{name[-1]}_us"] = _r(r["per_launch_s"] * 1e6)
             torch.cuda.empty_cache()
         for name in ("cfg4", "cfg5"):
             r = bench_msda_bwd(name, min(k2, 200), args.warmup, device, seed + 3, stream)
-            gbs = r["bytes"] / r["per_launch_s"] / 1e9
-            secondary[f"msda_bwd_{name}"] = {
-                "workload": MSDA_CFGS[name]["desc"].replace(" fwd", " bwd") +
-                            " (grad_value zeroing + backward kernel)",
-                "us_per_call": r["per_launch_s"] * 1e6,
-                "algorithmic_GBps": gbs, "frac_hbm_peak": gbs / peaks["hbm_gbs"],
-                "roofline_us": r["bytes"] / (peaks["hbm_gbs"] * 1e9) * 1e6,
-                "traffic": _traffic(f"msda_bwd {name}")}
+            legs[f"msda_bwd{name[-1]}_us"] = _r(r["per_launch_s"] * 1e6)
             torch.cuda.empty_cache()
         rc = bench_chain(min(k2, 20), args.warmup, device, seed + 6, stream, rank, world, dist)
-        secondary["chain_5"] = {
-            "workload": CHAIN_DESC, "images": CHAIN_IMAGES, "n_gpus": world,
-            "images_per_rank": rc["images_per_rank"], "ms_per_step": rc["per_step_s"] * 1e3,
-            "images_per_s": CHAIN_IMAGES / rc["per_step_s"], "scaling": "strong",
-            "verified": rc["verified"],
-            "verification": "per-image output checksums all-gathered to rank 0 outside the "
-                            "timed region and compared with rank 0's recomputation of every "
-                            "rank's block"}
+        legs["chain5_ms"] = _r(rc["per_step_s"] * 1e3)
+        legs["chain5_img_s"] = _r(CHAIN_IMAGES / rc["per_step_s"])
+        legs["chain5_ok"] = rc["verified"]
         torch.cuda.empty_cache()
 
     cpu = None
+    cpu_host = cpu_info()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tf, npix, calls, threads = cpu_dcn_sample(cfg_name, 3.5, seed)
-        cpu = {"value": tf, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-               "sample": f"C oracle (oracle/bevk_oracle.c) on {npix} of "
-                         f"{cfg['B'] * cfg['H'] * cfg['W']} output pixels of cfg2, median of "
-                         f"{calls} calls, fp32 math with double accumulation"}
+        c2 = cpu_dcn(cfg_name, 1.5, seed)
+        cpu = {"value": c2["tflops"], "unit": "TFLOP/s", "cores": c2["threads"], "kind": "port",
+               "sample": f"C oracle (oracle/bevk_oracle.c) on {c2['npix']} of {c2['M']} output "
+                         f"pixels of cfg2 per call, median of 5 after a warm-up, fp32 math "
+                         f"with double accumulation, {c2['threads']} threads on "
+                         f"{cpu_host['model']}"}
+        configs["cfg2"]["cpu_us"] = _r(c2["us"])
+        if not args.no_secondary:
+            for name in ("cfg1", "cfg3"):
+                c = cpu_dcn(name, 1.5, seed)
+                configs[name]["cpu_us"] = _r(c["us"])
+            for name in ("cfg4", "cfg5"):
+                c = cpu_msda(name, 1.5, seed)
+                configs[name]["cpu_us"] = _r(c["us"])
 
     if rank == 0:
         line = {
@@ -867,22 +1002,23 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded; BASELINE cfg2 shapes and distributions)",
-            "config": {"workload": cfg["desc"] + " (fp32 accumulate)",
-                       "global_batch": cfg["B"] * world, "parallelism": f"dp{world} "
-                       "(cameras sharded across ranks, no collective on the data path)",
-                       "l2": f"inputs rotate over {res['n_sets']} independent sets "
-                             f"({res['n_sets'] * nbytes / 2**20:.0f} MiB > 126 MB L2)"},
+            "config": headline_config(world),
             "roofline": roof,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "api": "modulated_deform_conv.modulated_deform_conv2d (pinned host in/out every step; H2D of step k+1 and D2H of step k-1 overlap step k on separate streams)",
-                    "clocks": e2e_clocks.summary()},
+                    "api": "modulated_deform_conv2d, pinned host in/out every step, copies "
+                           "overlapped on two streams"},
             "gpu_launches": args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
-            "secondary": secondary,
+            "cpu_host": cpu_host,
+            "legs": legs,
+            # per BASELINE config: device us/call, roofline fraction (tensor for
+            # DCN, HBM for MSDA; of measured peaks), e2e us/step (pinned host
+            # in/out), CPU oracle us/call (all host threads), fp16/bf16 MSDA
+            "configs": {k: configs[k] for k in sorted(configs)},
         }
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line, separators=(",", ":")), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
