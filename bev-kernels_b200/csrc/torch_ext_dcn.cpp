@@ -87,6 +87,58 @@ void modulated_deformable_im2col_nhwc_cuda(const Tensor data_im, const Tensor da
              dilation_h, dilation_w, deformable_group, data_col, 1);
 }
 
+void dcn_offset_conv_sum(const Tensor &partials, const c10::optional<Tensor> &offset_bias,
+                         Tensor offset_out, int64_t batch, int64_t height, int64_t width,
+                         int64_t kernel_h, int64_t kernel_w, int64_t stride_h, int64_t stride_w,
+                         int64_t pad_h, int64_t pad_w, int64_t dil_h, int64_t dil_w);
+
+// csrc/binding.cpp:72-78 / :167-169 (csrc/dcn_fused_nhwc_cuda.cu:92-126): the
+// Pack module's offset convolution and the deformable gather in one call.
+// data_im [B, H, W, Cin] contiguous, w_off [3T, T, Cin] (the offset conv's
+// weight [3T, Cin, kH, kW] permuted (0, 2, 3, 1)), b_off [3T] (fp32),
+// data_col [B*Ho*Wo, T*Cin] (k = t*Cin + ci), deformable_group 1.  The offset
+// conv's channel reduction runs as one GEMM with fp32 output, the tap sum and
+// bias in bevk_dcn_offset_conv_sum (rounded once to the input dtype, as the
+// unfused offset conv returns it), then the NHWC gather reads offsets and
+// mask logits from that output (sigmoid applied on load).
+void modulated_deformable_fused_im2col_nhwc_cuda(const Tensor data_im, const Tensor w_off,
+                                                 const Tensor b_off, int batch_size, int channels,
+                                                 int height_im, int width_im, int height_col,
+                                                 int width_col, int kernel_h, int kernel_w,
+                                                 int pad_h, int pad_w, int stride_h, int stride_w,
+                                                 int dilation_h, int dilation_w,
+                                                 int deformable_group, Tensor data_col) {
+  TORCH_CHECK(deformable_group == 1, "bevk: the NHWC fused path supports deformable_group == 1");
+  check_cuda(data_im, "data_im");
+  check_same_device(data_im, w_off, "w_off");
+  check_same_device(data_im, b_off, "b_off");
+  check_same_device(data_im, data_col, "data_col");
+  const int64_t T = int64_t(kernel_h) * kernel_w;
+  const int64_t C3 = 3 * T;
+  TORCH_CHECK(data_im.dim() == 4 && data_im.is_contiguous() && data_im.size(0) == batch_size &&
+                  data_im.size(1) == height_im && data_im.size(2) == width_im &&
+                  data_im.size(3) == channels,
+              "bevk: data_im must be contiguous NHWC [B, H, W, Cin]");
+  TORCH_CHECK(w_off.scalar_type() == data_im.scalar_type() && w_off.numel() == C3 * T * channels,
+              "bevk: w_off must be [3*kH*kW, kH*kW, Cin] in data_im's dtype");
+  TORCH_CHECK(b_off.numel() == C3, "bevk: b_off must have 3*kH*kW elements");
+  const c10::cuda::CUDAGuard guard(data_im.device());
+  // GEMM operand [ld, Cin]: row t*3T + c = w_off[c, t, :], zero rows up to ld
+  const int64_t n = T * C3, ld = (n + 31) / 32 * 32;
+  Tensor wz = at::zeros({ld, channels}, data_im.options());
+  wz.narrow(0, 0, n).copy_(w_off.reshape({C3, T, channels}).permute({1, 0, 2}).reshape({n, channels}));
+  const Tensor x2 = data_im.reshape({int64_t(batch_size) * height_im * width_im, channels});
+  const Tensor partials = data_im.scalar_type() == at::kFloat
+                              ? at::mm(x2, wz.t())
+                              : at::mm(x2, wz.t(), at::kFloat);
+  Tensor y = at::empty({batch_size, height_col, width_col, C3}, data_im.options());
+  dcn_offset_conv_sum(partials, b_off, y, batch_size, height_im, width_im, kernel_h, kernel_w,
+                      stride_h, stride_w, pad_h, pad_w, dilation_h, dilation_w);
+  col_common(data_im, y, y, batch_size, channels, height_im, width_im, height_col, width_col,
+             kernel_h, kernel_w, pad_h, pad_w, stride_h, stride_w, dilation_h, dilation_w, 1,
+             data_col, 1);
+}
+
 bevk_dcn_problem make_problem(const Tensor &input, const Tensor &offset, const Tensor &mask,
                               const Tensor &output, int64_t out_channels, int kernel_h,
                               int kernel_w, int stride_h, int stride_w, int pad_h, int pad_w,
@@ -562,6 +614,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Modulated deformable im2col, NCHW column matrix [C*kH*kW, B*Ho*Wo]");
   m.def("modulated_deformable_im2col_nhwc_cuda", &modulated_deformable_im2col_nhwc_cuda,
         "Modulated deformable gather, NHWC column matrix [B*Ho*Wo, kH*kW*C]");
+  m.def("modulated_deformable_fused_im2col_nhwc_cuda",
+        &modulated_deformable_fused_im2col_nhwc_cuda,
+        "Offset conv + deformable gather + sigmoid modulation -> Col [M, T*Cin], NHWC dg=1");
   m.def("dcn_pack_weight", &dcn_pack_weight, "Pack [Cout, Cin/g, kH, kW] weights",
         py::arg("weight"), py::arg("groups") = 1);
   m.def("dcn_offset_conv_sum", &dcn_offset_conv_sum,

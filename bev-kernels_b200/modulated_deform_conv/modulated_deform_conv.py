@@ -462,6 +462,11 @@ def dcn_backward(input, offset, mask, weight, grad_output, stride, padding, dila
 modulated_deform_conv2d = ModulatedDeformConv2dFunction.apply
 
 
+# The two module classes below keep mmcv's interface so that its checkpoints
+# load unchanged: constructor arguments, parameter names and shapes, weight
+# initialisation, the conv_offset layer and the version-1 state-dict key
+# migration follow mmcv.ops.ModulatedDeformConv2d(Pack) (Copyright (c)
+# OpenMMLab, Apache License 2.0; see NOTICE at the repository root).
 class ModulatedDeformConv2d(nn.Module):
     """Drop-in for mmcv.ops.ModulatedDeformConv2d (modulated_deform_conv.py:505-543)."""
 

@@ -50,10 +50,12 @@ def ms_deform_attn_backward(value: torch.Tensor, spatial_shapes: torch.Tensor,
                             attn_weight: torch.Tensor, grad_output: torch.Tensor, *,
                             im2col_step: int = 64, force_generic_col2im: bool = False):
     """-> (grad_value, grad_sampling_loc, grad_attn_weight), each in its
-    input's shape and dtype (dispatch.py:38-69 of the reference)."""
+    input's shape and dtype (dispatch.py:38-69 of the reference, which zeroes
+    all three; here only grad_value, which the kernel accumulates into -- the
+    kernel writes every element of the location and attention gradients)."""
     grad_value = torch.zeros_like(value)
-    grad_sampling_loc = torch.zeros_like(sampling_loc)
-    grad_attn_weight = torch.zeros_like(attn_weight)
+    grad_sampling_loc = torch.empty_like(sampling_loc)
+    grad_attn_weight = torch.empty_like(attn_weight)
     _load_ext().backward(value, spatial_shapes, level_start_index, sampling_loc, attn_weight,
                          grad_output, grad_value, grad_sampling_loc, grad_attn_weight,
                          im2col_step=im2col_step, force_generic_col2im=force_generic_col2im)

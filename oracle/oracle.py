@@ -193,16 +193,29 @@ def msda_forward(value, spatial_shapes, level_start_index, sampling_loc, attn_we
 
 
 _REF_PATH = os.path.join(_HERE, "_ref", "libmsda_ref.so")
-_REF_TREE = os.environ.get("BEVK_REFERENCE_DIR", "/root/reference")
+
+
+def reference_tree():
+    """The reference checkout, if there is one: $BEVK_REFERENCE_DIR, else a
+    directory named ``reference`` beside this repository; None otherwise."""
+    cand = os.environ.get("BEVK_REFERENCE_DIR") or os.path.join(
+        os.path.dirname(os.path.dirname(_HERE)), "reference")
+    return cand if os.path.isdir(os.path.join(cand, "csrc_musa", "msda")) else None
+
+
+def build_reference() -> bool:
+    """Compile the reference's MSDA kernels for the host into oracle/_ref
+    (`make -C oracle ref REF_DIR=...`) when the reference tree is present."""
+    tree = reference_tree()
+    if tree is not None:
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF_DIR={tree}"], check=False)
+    return os.path.exists(_REF_PATH)
 
 
 def reference_msda_available() -> bool:
     """Whether the reference's own MSDA kernel is built for the host
-    (oracle/_ref, `make -C oracle ref`); built here on demand when the
-    reference tree is present."""
-    if not os.path.exists(_REF_PATH) and os.path.isdir(_REF_TREE):
-        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF_DIR={_REF_TREE}"], check=False)
-    return os.path.exists(_REF_PATH)
+    (oracle/_ref); built here on demand when the reference tree is present."""
+    return os.path.exists(_REF_PATH) or build_reference()
 
 
 def reference_msda_forward(value, spatial_shapes, level_start_index, sampling_loc,

@@ -150,3 +150,33 @@ def test_cabi_offset_conv_contract(cuda):
     dcn_forward_into(xv, yv[:, :18], yv[:, 18:], w, b, want.permute(0, 3, 1, 2), 1, 1, 1,
                      mask_is_logit=True)
     assert torch.equal(out, want)
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16, torch.float32],
+                         ids=["f16", "bf16", "f32"])
+@pytest.mark.parametrize("geom", [((3, 3), 1, 1, 1), ((3, 3), 2, 2, 2)], ids=["s1", "s2d2"])
+def test_fused_im2col_nhwc_op(cuda, dt, geom):
+    """modulated_deformable_fused_im2col_nhwc_cuda (the reference's binding.cpp
+    :72-78): offset conv + gather + sigmoid modulation into Col [M, T*Cin],
+    against the offset conv in fp32 (rounded to the input dtype) and the
+    oracle's NHWC columns."""
+    import _modulated_deform_conv_ext as ext
+    k, stride, pad, dil = geom
+    B, C, H, W = 2, 64, 11, 14
+    x, w_off, b_off, _, _ = _inputs(9, B, C, H, W, 8, k, dt)
+    T = k[0] * k[1]
+    y = F.conv2d(x.permute(0, 3, 1, 2).float(), w_off.float(), b_off.float(), stride, pad, dil)
+    y = y.to(dt).float()
+    Ho, Wo = y.shape[2], y.shape[3]
+    want = torch.from_numpy(oracle.dcn_columns(
+        x.permute(0, 3, 1, 2).float().numpy(), y[:, :2 * T].numpy(),
+        torch.sigmoid(y[:, 2 * T:]).numpy(), k, stride, pad, dil, 1, layout="nhwc"))
+    col = torch.full((B * Ho * Wo, T * C), float("nan"), device=cuda, dtype=dt)
+    ext.modulated_deformable_fused_im2col_nhwc_cuda(
+        x.to(cuda).contiguous(), w_off.permute(0, 2, 3, 1).contiguous().to(cuda),
+        b_off.float().to(cuda), B, C, H, W, Ho, Wo, k[0], k[1], pad, pad, stride, stride, dil,
+        dil, 1, col)
+    torch.cuda.synchronize()
+    assert torch.isfinite(col).all()
+    tol = 1e-5 if dt == torch.float32 else HALF_REL
+    assert rel_l2(col.float(), want) <= tol, rel_l2(col.float(), want)

@@ -25,6 +25,7 @@ def test_extension_exports_reference_op_names():
     import _modulated_deform_conv_ext as ext
     for name in ("modulated_deformable_im2col_cuda", "modulated_deformable_im2col_opt_cuda",
                  "modulated_deformable_im2col_nhwc_cuda", "dcn_forward", "dcn_pack_weight",
+                 "modulated_deformable_fused_im2col_nhwc_cuda",
                  # backward ops, csrc/binding.cpp:146-191
                  "modulated_deformable_col2im_cuda", "modulated_deformable_col2im_opt_cuda",
                  "modulated_deformable_col2im_smem_cuda", "modulated_deformable_col2im_coord_cuda",
