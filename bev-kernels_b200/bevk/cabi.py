@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "bevk_status_string",
     "bevk_last_error_message",
     "bevk_device_watchdog",
+    "bevk_set_wait_limit_ns",
     "bevk_dcn_output_size",
     "bevk_dcn_packed_weight_bytes",
     "bevk_dcn_pack_weight",
@@ -134,6 +135,8 @@ def lib():
     L.bevk_last_error_message.restype = ctypes.c_char_p
     L.bevk_device_watchdog.restype = i
     L.bevk_device_watchdog.argtypes = [i, ctypes.POINTER(ctypes.c_uint)]
+    L.bevk_set_wait_limit_ns.restype = i
+    L.bevk_set_wait_limit_ns.argtypes = [i, ctypes.c_ulonglong]
     L.bevk_dcn_output_size.restype = i
     L.bevk_dcn_output_size.argtypes = [pp, ctypes.POINTER(i), ctypes.POINTER(i)]
     L.bevk_dcn_packed_weight_bytes.restype = sz

@@ -178,6 +178,11 @@ BEVK_API int bevk_device_watchdog(int device, unsigned int *code) {
   return read_and_clear_watchdog(device, code);
 }
 
+BEVK_API int bevk_set_wait_limit_ns(int device, unsigned long long ns) {
+  clear_error();
+  return set_wait_limit(device, ns);
+}
+
 // ------------------------------------------------------------------ DCN
 BEVK_API int bevk_dcn_output_size(const bevk_dcn_problem *p, int *height_out, int *width_out) {
   clear_error();

@@ -141,5 +141,9 @@ int launch_dcn_im2col(const bevk_dcn_problem *p, const DcnDims &d, const void *x
 
 // Device watchdog word (one per device, defined in dcn_tc.cu).
 int read_and_clear_watchdog(int device, unsigned int *code);
+// Limit of the fused DCN kernel's pipeline barrier waits on `device` (0: the
+// default 2 s); launches read it on the host and pass it to the kernel.
+int set_wait_limit(int device, unsigned long long ns);
+unsigned long long wait_limit(int device);
 
 }  // namespace bevk

@@ -66,19 +66,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 // Bounded wait on phase `parity` of `bar`.  Returns false (after recording
-// `site` in *err_word and raising *abort_flag) when the limit expires or when
-// another role of the same CTA already aborted.
+// `site` in *err_word and raising *abort_flag) when `limit_ns` expires or when
+// another role of the same CTA already aborted.  The clock and the abort flag
+// are read on every 256th retry; try_wait itself suspends the thread for a
+// hardware-defined interval, so a limit shorter than the default is also
+// checked on the first retry (otherwise a short wait could finish before the
+// limit is ever looked at).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   volatile int *abort_flag,
                                                   unsigned int *err_word,
-                                                  unsigned int site) {
+                                                  unsigned int site,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u) {
+    if ((it & 255u) == 0u || (it == 1u && limit_ns < kWaitLimitNs)) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         atomicCAS(err_word, 0u, site);
         *abort_flag = 1;
         return false;
@@ -103,14 +108,15 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 __device__ __forceinline__ bool mbar_wait_bounded_cluster(uint32_t bar, uint32_t parity,
                                                           volatile int *abort_flag,
                                                           unsigned int *err_word,
-                                                          unsigned int site) {
+                                                          unsigned int site,
+                                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((it & 255u) == 0u) {
+    if ((it & 255u) == 0u || (it == 1u && limit_ns < kWaitLimitNs)) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         atomicCAS(err_word, 0u, site);
         *abort_flag = 1;
         return false;

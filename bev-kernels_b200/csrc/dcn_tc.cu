@@ -33,6 +33,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 
@@ -73,6 +74,7 @@ struct TcParams {
   int mask_is_logit, has_bias, act_relu;
   int xs0, xs2, xs3;        // input strides (channel stride is 1)
   int64_t os[4], ms[4], ys[4];
+  unsigned long long wait_limit_ns;  // pipeline barrier waits (bevk_set_wait_limit_ns)
 };
 
 // Tile schedules of the fused kernel.
@@ -367,7 +369,8 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   // Barriers the gather warps and TMA copies report to: the leader's.
   const uint32_t full_dst = PAIR ? ptx::mapa_shared(bar_full, 0) : bar_full;
   auto wait = [&](uint32_t bar, uint32_t parity, unsigned int site) -> bool {
-    return ptx::mbar_wait_bounded(bar, parity, s_abort, &g_bevk_watchdog, site);
+    return ptx::mbar_wait_bounded(bar, parity, s_abort, &g_bevk_watchdog, site,
+                                  p.wait_limit_ns);
   };
 
   bool ok = true;
@@ -547,11 +550,12 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
         }
         issued = kit + 1;
       }
-      if (*s_abort && issued > 0) {
+      if (*s_abort && (issued > 0 || CLUSTER)) {
         // The copies issued here (and, clustered, the ones reporting to the
-        // other CTA) share their barriers with gather arrivals that an abort
-        // may have skipped, so no barrier phase is left to wait on: give
-        // them time to land before shared memory can be released.
+        // other CTA, and the gather warps' copies of A rows to the other CTA)
+        // share their barriers with arrivals that an abort may have skipped,
+        // so no barrier phase is left to wait on: give them time to land
+        // before shared memory can be released.
         for (int i = 0; i < 64; ++i) __nanosleep(2000);
       }
     }
@@ -847,6 +851,7 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
   p.mask_is_logit = pr->mask_is_logit;
   p.has_bias = pr->has_bias;
   p.act_relu = pr->act_relu;
+  p.wait_limit_ns = wait_limit(current_device());
   p.xs0 = static_cast<int>(xs[0]); p.xs2 = static_cast<int>(xs[2]); p.xs3 = static_cast<int>(xs[3]);
   for (int i = 0; i < 4; ++i) {
     p.os[i] = pr->offset_strides[i];
@@ -899,10 +904,38 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
   return go(TypeTag<__nv_bfloat16>{});
 }
 
+namespace {
+// Per-device limit of the fused kernel's pipeline barrier waits, passed to
+// every launch (0 = the default).
+constexpr int kMaxWaitDevices = 64;
+std::atomic<unsigned long long> g_wait_limit_ns[kMaxWaitDevices];
+}  // namespace
+
+unsigned long long wait_limit(int device) {
+  const unsigned long long v =
+      device >= 0 && device < kMaxWaitDevices ? g_wait_limit_ns[device].load() : 0ull;
+  return v ? v : ptx::kWaitLimitNs;
+}
+
+int set_wait_limit(int device, unsigned long long ns) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail(BEVK_ERR_CUDA, "wait limit: no CUDA device");
+  }
+  if (device < 0 || device >= n || device >= kMaxWaitDevices)
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "wait limit: bad device %d", device);
+  g_wait_limit_ns[device].store(ns);
+  return BEVK_OK;
+}
+
 int read_and_clear_watchdog(int device, unsigned int *code) {
   int prev = -1;
   cudaGetDevice(&prev);
-  if (cudaSetDevice(device) != cudaSuccess) return fail(BEVK_ERR_INVALID_ARGUMENT, "watchdog: bad device %d", device);
+  if (cudaSetDevice(device) != cudaSuccess) {
+    (void)cudaGetLastError();  // leave no error pending for later launch checks
+    return fail(BEVK_ERR_INVALID_ARGUMENT, "watchdog: bad device %d", device);
+  }
   unsigned int v = 0, zero = 0;
   cudaError_t e = cudaDeviceSynchronize();
   if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_bevk_watchdog, sizeof(v));

@@ -76,6 +76,17 @@ BEVK_API const char *bevk_last_error_message(void);
 BEVK_API int bevk_device_watchdog(int device, unsigned int *code);
 
 /*
+ * Diagnostics, no counterpart in the reference: sets the time limit of the
+ * fused DCN forward kernel's pipeline barrier waits on `device` to `ns`
+ * nanoseconds (0 restores the default, 2 s).  The teardown waits that drain
+ * tensor-core work and copies before a CTA releases its memory keep the
+ * default.  With a short limit, launches give up mid-pipeline: the kernel
+ * unwinds, writes no output and records the site in the watchdog word above.
+ * For tests of that path.  Applies to launches made after the call.
+ */
+BEVK_API int bevk_set_wait_limit_ns(int device, unsigned long long ns);
+
+/*
  * Launch order.  The library's kernels are launched as programmatic
  * dependents of the stream's previous kernel: their set-up (barriers, tensor
  * memory, descriptor prefetch) may overlap that kernel's last CTAs, and each
