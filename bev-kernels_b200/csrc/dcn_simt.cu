@@ -16,6 +16,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "bevk_internal.h"
@@ -211,6 +212,169 @@ dcn_fwd_simt_kernel(SimtParams p, const T *__restrict__ x, const T *__restrict__
   }
 }
 
+// ---------------------------------------------------------------- small problems
+// Small problems (few 64 x 64 tiles, e.g. 1 x 64 x 32 x 32): a CTA owns SBM = 16
+// output pixels x 64 output channels, so four times as many CTAs run; the
+// reduction walks chunks of up to SBK = 64 channels (one chunk a tap when
+// Cin_g <= 64); the geometry of every (tap, deformable group) of the CTA's
+// pixels is computed once up front; and the next chunk's samples and weights
+// are loaded into registers while the current chunk's products accumulate, so
+// each chunk costs about one global-memory latency.  Same arithmetic as the
+// large kernel (fp32/fp64 sampling, Acc accumulation), same results.
+constexpr int SBM = 16, SBK = 64;
+constexpr int kSmallA = SBM * SBK / NT;   // gathered samples a thread loads per chunk
+constexpr int kSmallB = BN * SBK / NT;    // weights a thread loads per chunk
+
+template <typename T, typename Acc>
+__global__ void __launch_bounds__(NT)
+dcn_fwd_simt_small_kernel(SimtParams p, const T *__restrict__ x, const T *__restrict__ off,
+                          const T *__restrict__ msk, const T *__restrict__ wpk,
+                          const T *__restrict__ bias, T *__restrict__ y) {
+  // dynamic shared memory: the double-buffered A / B chunks, then the
+  // geometry [T * dg][SBM]
+  extern __shared__ __align__(16) unsigned char simt_small_smem[];
+  using ATile = Acc[SBK][SBM + 1];
+  using BTile = Acc[SBK][BN + 4];
+  ATile *s_a = reinterpret_cast<ATile *>(simt_small_smem);
+  BTile *s_b = reinterpret_cast<BTile *>(simt_small_smem + 2 * sizeof(ATile));
+  TapGeom<Acc> *s_geo =
+      reinterpret_cast<TapGeom<Acc> *>(simt_small_smem + 2 * sizeof(ATile) + 2 * sizeof(BTile));
+
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * SBM;
+  const int n_tiles_g = (p.Cout_g + BN - 1) / BN;
+  const int grp = blockIdx.y / n_tiles_g;
+  const int n0 = (blockIdx.y - grp * n_tiles_g) * BN;
+  const int c_base = grp * p.Cin_g;
+  const bool cl = p.xs[1] == 1;   // channel-contiguous input: channels fastest across threads
+
+  // geometry of every (tap, deformable group) x pixel of this tile
+  const int n_geo = p.T * (p.Cin / p.cpdg);   // taps x deformable groups
+  for (int e = tid; e < n_geo * SBM; e += NT) {
+    const int tg = e / SBM, r = e - (e / SBM) * SBM;
+    const int t = tg % p.T, dgi = tg / p.T;
+    s_geo[e] = tap_geometry<Acc>(p, off, msk, m0 + r, t, dgi);
+  }
+  __syncthreads();
+
+  // chunk k -> (tap t, channels [c0, c1) of the group, never crossing a
+  // deformable group); chunks are walked tap-major like the large kernel
+  struct Chunk {
+    int t, c0, c1, dgi;
+  };
+  auto chunk_at = [&](int t, int c0) {
+    const int cg = c_base + c0;
+    const int dgi = cg / p.cpdg;
+    const int dg_end = (dgi + 1) * p.cpdg - c_base;
+    return Chunk{t, c0, min(min(c0 + SBK, p.Cin_g), dg_end), dgi};
+  };
+  auto next_chunk = [&](Chunk c, bool &more) {
+    if (c.c1 < p.Cin_g) return chunk_at(c.t, c.c1);
+    if (c.t + 1 < p.T) return chunk_at(c.t + 1, 0);
+    more = false;
+    return c;
+  };
+  Acc ra[kSmallA], rb[kSmallB];
+  auto load = [&](const Chunk &c) {
+    const int clen = c.c1 - c.c0;
+    const TapGeom<Acc> *geo = s_geo + (c.dgi * p.T + c.t) * SBM;
+    // every corner load is issued before any is used: a dropped corner has
+    // offset 0 (a valid address) and weight 0, and is skipped in the sum
+    Acc raw[kSmallA][4];
+#pragma unroll
+    for (int i = 0; i < kSmallA; ++i) {
+      const int e = tid + i * NT;
+      const int r = cl ? e / SBK : e % SBM;
+      const int ci = cl ? e % SBK : e / SBM;
+      const TapGeom<Acc> &g = geo[r];
+      const int64_t co = static_cast<int64_t>(c_base + c.c0 + min(ci, clen - 1)) * p.xs[1];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) raw[i][q] = ld_acc<Acc>(x + g.off[q] + co);
+    }
+#pragma unroll
+    for (int i = 0; i < kSmallA; ++i) {
+      const int e = tid + i * NT;
+      const int r = cl ? e / SBK : e % SBM;
+      const int ci = cl ? e % SBK : e / SBM;
+      const TapGeom<Acc> &g = geo[r];
+      Acc v = Acc(0);
+      if (ci < clen) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (g.w[q] != Acc(0)) v += g.w[q] * raw[i][q];
+      }
+      ra[i] = v;
+    }
+#pragma unroll
+    for (int i = 0; i < kSmallB; ++i) {
+      const int e = tid + i * NT;
+      const int n = e / SBK, ci = e - (e / SBK) * SBK;
+      const int co = n0 + n;
+      Acc v = Acc(0);
+      if (ci < clen && co < p.Cout_g)
+        v = ld_acc<Acc>(wpk + (static_cast<int64_t>(grp) * p.Cout_g + co) * p.T * p.Cin_g_pad +
+                        static_cast<int64_t>(c.t) * p.Cin_g_pad + c.c0 + ci);
+      rb[i] = v;
+    }
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < kSmallA; ++i) {
+      const int e = tid + i * NT;
+      const int r = cl ? e / SBK : e % SBM;
+      const int ci = cl ? e % SBK : e / SBM;
+      s_a[buf][ci][r] = ra[i];
+    }
+#pragma unroll
+    for (int i = 0; i < kSmallB; ++i) {
+      const int e = tid + i * NT;
+      s_b[buf][e % SBK][e / SBK] = rb[i];
+    }
+  };
+
+  Acc acc[4] = {Acc(0), Acc(0), Acc(0), Acc(0)};
+  Chunk cur = chunk_at(0, 0);
+  load(cur);
+  store(0);
+  __syncthreads();
+  int buf = 0;
+  bool more = true;
+  while (true) {
+    const Chunk nxt = next_chunk(cur, more);
+    if (more) load(nxt);          // in flight while this chunk accumulates
+    const int clen = cur.c1 - cur.c0;
+    for (int k = 0; k < clen; ++k) {
+      const Acc a = s_a[buf][k][ty];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) acc[jj] += a * s_b[buf][k][tx * 4 + jj];
+    }
+    if (!more) break;
+    store(buf ^ 1);
+    __syncthreads();
+    buf ^= 1;
+    cur = nxt;
+  }
+
+  const int64_t m = m0 + ty;
+  if (m >= p.M) return;
+  const int64_t HoWo = static_cast<int64_t>(p.Ho) * p.Wo;
+  const int b = static_cast<int>(m / HoWo);
+  const int rem = static_cast<int>(m - b * HoWo);
+  const int oh = rem / p.Wo, ow = rem - (rem / p.Wo) * p.Wo;
+  T *yb = y + b * p.ys[0] + oh * p.ys[2] + ow * p.ys[3];
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    const int co = n0 + tx * 4 + jj;
+    if (co >= p.Cout_g) continue;
+    const int cog = grp * p.Cout_g + co;
+    Acc v = acc[jj];
+    if (p.has_bias) v += ld_acc<Acc>(bias + cog);
+    if (p.act_relu && v < Acc(0)) v = Acc(0);
+    yb[static_cast<int64_t>(cog) * p.ys[1]] = store_cast<T, Acc>(v);
+  }
+}
+
 // ---------------------------------------------------------------- packing
 // wpk[co][t][c] = weight[co][c][t] for c < Cin_g, 0 for the padding.
 template <typename T>
@@ -376,6 +540,33 @@ int launch_simt_typed(const bevk_dcn_problem *pr, const DcnDims &d, const void *
   if (mt > 0x7FFFFFFF || nt > 65535)
     return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn simt: grid (%lld x %lld) too large",
                 static_cast<long long>(mt), static_cast<long long>(nt));
+  // Fewer 64 x 64 tiles than two per SM: the small-tile kernel (its up-front
+  // geometry of every (tap, deformable group) must fit in 48 KB).
+  const int sms = device_info(current_device()).sm_count > 0
+                      ? device_info(current_device()).sm_count : 148;
+  const size_t geo_bytes = sizeof(TapGeom<Acc>) * SBM * d.T * d.dg;
+  if (mt * nt < 2 * sms && geo_bytes <= 48 * 1024) {
+    const size_t tiles = 2 * sizeof(Acc) * SBK * ((SBM + 1) + (BN + 4));
+    const size_t smem = tiles + geo_bytes;
+    constexpr int kMaxDevices = 64;
+    static std::atomic<bool> sized[kMaxDevices];
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices || !sized[dev].load(std::memory_order_relaxed)) {
+      if (cudaFuncSetAttribute(dcn_fwd_simt_small_kernel<T, Acc>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(tiles + 48 * 1024)) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return fail(BEVK_ERR_CUDA, "dcn simt: cannot size shared memory");
+      }
+      if (dev >= 0 && dev < kMaxDevices) sized[dev].store(true, std::memory_order_relaxed);
+    }
+    const int64_t smt = (d.M + SBM - 1) / SBM;
+    dim3 sgrid(static_cast<unsigned>(smt), static_cast<unsigned>(nt));
+    dcn_fwd_simt_small_kernel<T, Acc><<<sgrid, NT, smem, stream>>>(
+        p, static_cast<const T *>(x), static_cast<const T *>(off), static_cast<const T *>(msk),
+        static_cast<const T *>(wpk), static_cast<const T *>(bias), static_cast<T *>(y));
+    return check_launch("dcn_fwd_simt_small_kernel");
+  }
   dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt));
   dcn_fwd_simt_kernel<T, Acc><<<grid, NT, 0, stream>>>(
       p, static_cast<const T *>(x), static_cast<const T *>(off), static_cast<const T *>(msk),

@@ -175,6 +175,30 @@ def test_fp64_and_grouped_simt(cuda):
     assert rel_l2(out, want) <= FP32_REL
 
 
+SIMT_CASES = [
+    # B, C, H, W, Cout, groups, dg, layout: the small-tile kernel (fewer 64 x 64
+    # tiles than two per SM) and, for 313 tiles, the large-tile kernel
+    (1, 64, 32, 32, 64, 1, 1, "nchw"),
+    (2, 40, 17, 23, 72, 2, 4, "nchw"),          # chunks end at deformable-group edges
+    (1, 96, 9, 14, 130, 1, 1, "channels_last"),  # 96 = a full and a partial chunk
+    (2, 32, 100, 100, 64, 1, 1, "nchw"),        # large-tile kernel
+]
+
+
+@pytest.mark.parametrize("case", SIMT_CASES, ids=["cfg1", "g2dg4", "c96_cl", "large"])
+def test_fp32_simt_kernels(cuda, case):
+    B, C, H, W, Cout, groups, dg, layout = case
+    x, off, mask, w, b = dcn_inputs(17, B, C, H, W, Cout, groups=groups, dg=dg, off_std=1.0)
+    want = _oracle(x, off, mask, w, b, 1, 1, 1, groups=groups, dg=dg)
+    x, off, mask, w, b = (t.to(cuda) for t in (x, off, mask, w, b))
+    if layout == "channels_last":
+        x = x.contiguous(memory_format=torch.channels_last)
+    out = torch.full(want.shape, float("nan"), device=cuda)
+    cabi_dcn_forward(x, off, mask, w, b, out, (1, 1), (1, 1), (1, 1), groups=groups, dg=dg)
+    torch.cuda.synchronize()
+    assert rel_l2(out, want) <= FP32_REL and max_abs(out, want) <= FP32_ABS
+
+
 def test_im2col_compat_ops(cuda):
     """Reference extension column ops vs the reference goldens' column matrices."""
     import _modulated_deform_conv_ext as ext
