@@ -759,6 +759,36 @@ def cpu_msda(cfg_name, target_s, seed):
                 threads=oracle.max_threads())
 
 
+def cpu_torch_golden(cfg_name, seed):
+    """The reference's golden semantics on CPU through PyTorch, all host
+    threads, median of 5 calls after a warm-up: DCN as
+    torchvision.ops.deform_conv2d (bit-identical to the reference's golden,
+    modulated_deform_conv.py:216-266 + mm, on fp32), MSDA as the grid_sample
+    formulation (oracle/msda_grid_sample.py).  fp16/bf16 configs run in fp32
+    on the up-cast inputs.  Returns us per call, or None when torchvision is
+    missing."""
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    if cfg_name in DCN_CFGS:
+        try:
+            from torchvision.ops import deform_conv2d
+        except ImportError:
+            return None
+        cfg = DCN_CFGS[cfg_name]
+        st = dcn_sets(cfg, 1, seed, 0, torch.device("cpu"))[0]
+        x, off, mask, w = (st[k].float().contiguous() for k in ("x", "off", "mask", "w"))
+        b = None if st["b"] is None else st["b"].float()
+        with torch.no_grad():
+            t = _median_calls(lambda i: deform_conv2d(x, off, w, b, (1, 1), (1, 1), (1, 1), mask))
+    else:
+        from oracle.msda_grid_sample import msda_forward_grid_sample
+        st = msda_sets(MSDA_CFGS[cfg_name], 1, seed, torch.device("cpu"))[0]
+        with torch.no_grad():
+            t = _median_calls(lambda i: msda_forward_grid_sample(st["value"], st["shapes"],
+                                                                 st["loc"], st["attn"]))
+    return t * 1e6
+
+
 def headline_config(world):
     """The headline's `config` (shared by both arms, so the driver can compare
     them): BASELINE cfg2, weak-scaled over the ranks."""
@@ -988,13 +1018,16 @@ def main():
                          f"with double accumulation, {c2['threads']} threads on "
                          f"{cpu_host['model']}"}
         configs["cfg2"]["cpu_us"] = _r(c2["us"])
+        configs["cfg2"]["cpu_torch_us"] = _r(cpu_torch_golden("cfg2", seed))
         if not args.no_secondary:
             for name in ("cfg1", "cfg3"):
                 c = cpu_dcn(name, 1.5, seed)
                 configs[name]["cpu_us"] = _r(c["us"])
+                configs[name]["cpu_torch_us"] = _r(cpu_torch_golden(name, seed))
             for name in ("cfg4", "cfg5"):
                 c = cpu_msda(name, 1.5, seed)
                 configs[name]["cpu_us"] = _r(c["us"])
+                configs[name]["cpu_torch_us"] = _r(cpu_torch_golden(name, seed))
 
     if rank == 0:
         line = {
@@ -1015,7 +1048,10 @@ def main():
             "legs": legs,
             # per BASELINE config: device us/call, roofline fraction (tensor for
             # DCN, HBM for MSDA; of measured peaks), e2e us/step (pinned host
-            # in/out), CPU oracle us/call (all host threads), fp16/bf16 MSDA
+            # in/out), CPU us/call on all host threads -- the C oracle
+            # (cpu_us) and the reference's golden semantics through PyTorch
+            # (cpu_torch_us: torchvision deform_conv2d / grid_sample MSDA) --
+            # and fp16/bf16 MSDA
             "configs": {k: configs[k] for k in sorted(configs)},
         }
         print(json.dumps(line, separators=(",", ":")), flush=True)
