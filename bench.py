@@ -886,7 +886,7 @@ def main():
                                        "bwd_cfg3", "bwd_cfg4", "bwd_cfg5", "pack_cfg2",
                                        "pack_cfg3", "chain"),
                     help="time one workload's kernel only (profiling runs: no e2e, "
-                         "secondary or CPU legs; prints a reduced line)")
+                         "legs, per-config record or CPU legs; prints a reduced line)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
