@@ -109,6 +109,8 @@ void modulated_deformable_fused_im2col_nhwc_cuda(const Tensor data_im, const Ten
                                                  int dilation_h, int dilation_w,
                                                  int deformable_group, Tensor data_col) {
   TORCH_CHECK(deformable_group == 1, "bevk: the NHWC fused path supports deformable_group == 1");
+  TORCH_CHECK(int64_t(kernel_h) * kernel_w <= 9,
+              "bevk: the fused offset-conv gather supports kernels of at most 9 taps");
   check_cuda(data_im, "data_im");
   check_same_device(data_im, w_off, "w_off");
   check_same_device(data_im, b_off, "b_off");
