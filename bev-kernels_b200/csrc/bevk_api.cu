@@ -211,11 +211,19 @@ BEVK_API int bevk_dcn_pack_weight(const bevk_dcn_problem *p, const void *weight,
                                 reinterpret_cast<cudaStream_t>(stream));
 }
 
+// Forward scratch: [NHWC copy of an input that is not channel-contiguous,
+// rounded up to 256 bytes][the tensor-core kernel's K-split scratch].
+static size_t transpose_bytes(const bevk_dcn_problem *p, const DcnDims &d) {
+  if (!input_needs_transpose(p)) return 0;
+  return (static_cast<size_t>(d.B) * d.H * d.W * d.Cin * dtype_size(p->dtype) + 255) &
+         ~static_cast<size_t>(255);
+}
+
 BEVK_API size_t bevk_dcn_forward_workspace_bytes(const bevk_dcn_problem *p) {
   DcnDims d;
   if (dcn_dims(p, &d) != BEVK_OK) return 0;
-  if (!dcn_tc_supported(p, d) || !input_needs_transpose(p)) return 0;
-  return static_cast<size_t>(d.B) * d.H * d.W * d.Cin * dtype_size(p->dtype);
+  if (!dcn_tc_supported(p, d)) return 0;
+  return transpose_bytes(p, d) + dcn_tc_workspace_bytes(p, d);
 }
 
 BEVK_API int bevk_dcn_offset_conv_sum(const bevk_dcn_problem *p, const bevk_dcn_zoff_args *z,
@@ -270,11 +278,18 @@ BEVK_API int bevk_dcn_forward(const bevk_dcn_problem *p, const void *input, cons
     const void *x = input;
     int64_t xs[4] = {p->input_strides[0], p->input_strides[1], p->input_strides[2],
                      p->input_strides[3]};
+    // the K-split scratch follows the transposed input (optional: without it
+    // the kernel takes a schedule that needs none)
+    void *tail = workspace;
+    size_t tail_bytes = workspace ? workspace_bytes : 0;
     if (input_needs_transpose(p)) {
       const size_t need = static_cast<size_t>(d.B) * d.H * d.W * d.Cin * dtype_size(p->dtype);
       if (!workspace || workspace_bytes < need || !aligned(workspace, 16))
         return fail(BEVK_ERR_WORKSPACE, "dcn_forward: needs a 16-byte aligned workspace of %zu bytes",
                     need);
+      const size_t used = transpose_bytes(p, d);
+      tail = workspace_bytes > used ? static_cast<char *>(workspace) + used : nullptr;
+      tail_bytes = workspace_bytes > used ? workspace_bytes - used : 0;
       st = launch_nchw_to_nhwc(input, workspace, d.B, d.Cin, d.H, d.W, p->input_strides, p->dtype, s);
       if (st != BEVK_OK) return st;
       x = workspace;
@@ -283,7 +298,8 @@ BEVK_API int bevk_dcn_forward(const bevk_dcn_problem *p, const void *input, cons
       xs[2] = static_cast<int64_t>(d.W) * d.Cin;
       xs[3] = d.Cin;
     }
-    st = launch_dcn_forward_tc(p, d, x, xs, offset, mask, packed_weight, bias, output, s);
+    st = launch_dcn_forward_tc(p, d, x, xs, offset, mask, packed_weight, bias, output, tail,
+                               tail_bytes, s);
     if (st != BEVK_ERR_INDEX_OVERFLOW && st != BEVK_ERR_MISALIGNED) return st;
     clear_error();  // geometry the tensor-core kernel cannot index: exact path below
   }

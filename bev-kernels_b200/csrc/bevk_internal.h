@@ -121,11 +121,16 @@ int launch_dcn_forward_simt(const bevk_dcn_problem *p, const DcnDims &d,
 // Tensor-core path: x must be channel-contiguous (c stride 1) with 16-byte
 // aligned pixel rows; returns BEVK_ERR_UNSUPPORTED when the geometry is not
 // covered so the caller can pick the SIMT kernel.
+// `ws` (may be null) is scratch for the K-split schedule, used when it holds
+// dcn_tc_workspace_bytes(p, d) bytes at a 256-byte boundary; without it the
+// kernel takes a schedule that needs none.
 bool dcn_tc_supported(const bevk_dcn_problem *p, const DcnDims &d);
+size_t dcn_tc_workspace_bytes(const bevk_dcn_problem *p, const DcnDims &d);
 int launch_dcn_forward_tc(const bevk_dcn_problem *p, const DcnDims &d,
                           const void *x, const int64_t x_strides[4],
                           const void *off, const void *msk, const void *wpk,
-                          const void *bias, void *out, cudaStream_t stream);
+                          const void *bias, void *out, void *ws, size_t ws_bytes,
+                          cudaStream_t stream);
 
 // Offset convolution from its per-tap partial products (see
 // bevk_dcn_zoff_args): y[m, c] = round(bias[c] + sum_t z[p_t(m) * ld + t*3T + c]),

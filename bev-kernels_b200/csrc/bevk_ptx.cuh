@@ -92,6 +92,30 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// Device-scope exchange / release store / acquire load of 64-bit words in
+// global memory (CTAs of one grid meeting on a ticket), and the grid's
+// temporal launch number (distinct for every launch in a context).
+__device__ __forceinline__ unsigned long long atom_exch_acq_rel_gpu(unsigned long long *p,
+                                                                    unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.acq_rel.gpu.global.exch.b64 %0, [%1], %2;"
+               : "=l"(old) : "l"(p), "l"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long grid_id() {
+  unsigned long long g;
+  asm volatile("mov.u64 %0, %%gridid;" : "=l"(g));
+  return g;
+}
+
 // Cluster-scope variants (paired-CTA kernels): a wait that must observe
 // arrivals released by the other CTA of the cluster.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {

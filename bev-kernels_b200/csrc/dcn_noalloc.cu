@@ -120,7 +120,7 @@ extern "C" BEVK_API int bevk_dcn_forward_noalloc(const bevk_dcn_problem *p, cons
       xs[2] = static_cast<int64_t>(d.W) * d.Cin;
       xs[3] = d.Cin;
     }
-    st = launch_dcn_forward_tc(p, d, x, xs, offset, mask, wpk, bias, output, s);
+    st = launch_dcn_forward_tc(p, d, x, xs, offset, mask, wpk, bias, output, nullptr, 0, s);
     if (st != BEVK_ERR_INDEX_OVERFLOW && st != BEVK_ERR_MISALIGNED) return st;
     clear_error();
   }

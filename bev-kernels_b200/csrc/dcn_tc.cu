@@ -58,6 +58,7 @@ constexpr int kBK = 64;            // channels per stage (128 B of fp16/bf16)
 constexpr int kGatherWarps = 16;
 constexpr int kEpilogueWarps = 16;  // warps 0-15: four per TMEM lane quadrant (w % 4)
 constexpr int kMaxTaps = 9;
+constexpr int kSplitCols = 256;     // K split: accumulator columns each half finishes
 
 // Watchdog sites (low byte) -- identify which wait expired.
 enum : unsigned int {
@@ -65,6 +66,7 @@ enum : unsigned int {
   kSiteTmaEmpty = 0xB0C2,
   kSiteMmaFull = 0xB0C3,
   kSiteEpilogue = 0xB0C4,
+  kSiteSplitK = 0xB0C5,
 };
 
 struct TcParams {
@@ -75,6 +77,14 @@ struct TcParams {
   int xs0, xs2, xs3;        // input strides (channel stride is 1)
   int64_t os[4], ms[4], ys[4];
   unsigned long long wait_limit_ns;  // pipeline barrier waits (bevk_set_wait_limit_ns)
+  // K split (kModePairN2): clusters [tile][k_split] each run stages
+  // [k_part * k_len, ...) of the tile; the two halves of a tile exchange half
+  // of their fp32 accumulators through `part` (per (tile, rank, half):
+  // [kSplitCols / 4][kBM][4] floats) and meet on `tickets` (two words per
+  // (tile, rank): arrival, release).
+  int k_split, k_len;
+  float *part;
+  unsigned long long *tickets;
 };
 
 // Tile schedules of the fused kernel.
@@ -82,6 +92,7 @@ enum : int {
   kModeSingle = 0,  // one CTA per 128-pixel x BN tile, M=128 MMA
   kModePair = 1,    // 2-CTA cluster per 256-pixel x BN tile, M=256 cta_group::2 MMA
   kModeNSplit = 2,  // 2-CTA cluster per 128-pixel x 2*BN tile, A rows shared
+  kModePairN2 = 3,  // 2-CTA cluster per 256-pixel x 2*BN tile: two M=256 accumulators
 };
 
 // Warp roles.  A warp issues on SM sub-partition (warp index mod 4).
@@ -132,10 +143,11 @@ __host__ __device__ constexpr int warps_per_stage() {
              : kGatherWarps;
 }
 
-template <int BN, int STAGES, bool PAIR>
+template <int BN, int STAGES, bool PAIR, int NH = 1>
 struct Smem {
-  // In a CTA pair each CTA holds half of the B tile (BN/2 output channels).
-  static constexpr int kBRows = PAIR ? BN / 2 : BN;
+  // In a CTA pair each CTA holds half of the B tile (BN/2 output channels) of
+  // each of the NH accumulators.
+  static constexpr int kBRows = PAIR ? NH * BN / 2 : BN;
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = kBRows * kBK * 2;
   static constexpr int kA = 0;
@@ -280,13 +292,16 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
                                                 const T *__restrict__ off,
                                                 const T *__restrict__ msk,
                                                 const T *__restrict__ bias, T *__restrict__ y) {
-  constexpr bool PAIR = MODE == kModePair;
+  constexpr bool N2 = MODE == kModePairN2;
+  constexpr bool PAIR = MODE == kModePair || N2;
   constexpr bool NSPLIT = MODE == kModeNSplit;
+  constexpr int NH = N2 ? 2 : 1;        // accumulators (N halves) per tile
+  constexpr int NCOLS = NH * BN;        // output channels per tile and TMEM columns
   constexpr bool CLUSTER = MODE != kModeSingle;
   constexpr int kGRows = NSPLIT ? kBM / 2 : kBM;   // A rows this CTA gathers per stage
   constexpr uint32_t kGBytes = kGRows * 128;       // their bytes in an A stage (copied
                                                    // to the other CTA under NSPLIT)
-  using L = Smem<BN, STAGES, PAIR>;
+  using L = Smem<BN, STAGES, PAIR, NH>;
   using GM = GatherMath<T>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -313,7 +328,12 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   const int gw = R::gather_index(warp);      // gather warp index 0..15
   const uint32_t cr = CLUSTER ? ptx::cluster_ctarank() : 0u;   // rank in the CTA pair
   const bool leader = cr == 0;
-  const int tile = CLUSTER ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int cl = CLUSTER ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  // K split: the clusters of one tile are adjacent, so they start together
+  const int k_part = N2 ? cl % p.k_split : 0;
+  const int tile = N2 ? cl / p.k_split : cl;
+  const int k_begin = N2 ? k_part * p.k_len : 0;             // first stage of this cluster
+  const int n_loc = N2 ? min(p.n_k - k_begin, p.k_len) : p.n_k;   // its stages (>= 1)
   const int n_tile = tile % p.n_tiles_n;
   const int m_tile = tile / p.n_tiles_n;
   // K order: stage kit covers tap kit % T of channel chunk kit / T.  Taps vary
@@ -321,7 +341,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   // across consecutive stages.  (Starting each tile at a different K offset
   // spreads the weight-tile reads over L2 but measured slower on B200.)
   const int m0 = PAIR ? m_tile * 2 * kBM + static_cast<int>(cr) * kBM : m_tile * kBM;
-  const int n0 = NSPLIT ? n_tile * 2 * BN + static_cast<int>(cr) * BN : n_tile * BN;
+  const int n0 = NSPLIT ? n_tile * 2 * BN + static_cast<int>(cr) * BN : n_tile * NCOLS;
   const int g_row0 = NSPLIT ? static_cast<int>(cr) * kGRows : 0;  // first tile row gathered here
 
   // The prologue below (barriers, TMEM, descriptor prefetch) touches no
@@ -343,7 +363,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   if constexpr (CLUSTER) ptx::cluster_sync();
   if (warp == R::kMma) {
     if constexpr (PAIR) {
-      ptx::tmem_alloc_pair(ptx::smem_u32(s_tmem_slot), BN);
+      ptx::tmem_alloc_pair(ptx::smem_u32(s_tmem_slot), NCOLS);
       ptx::tmem_relinquish_pair();
     } else {
       ptx::tmem_alloc(ptx::smem_u32(s_tmem_slot), BN);
@@ -505,16 +525,17 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
     {
       Prefetch A, B;
       StageCoord sc{0, 0};
+      if constexpr (N2) sc = StageCoord{k_begin % p.T, k_begin / p.T};
       for (int g = 0; g < grp; ++g)
         if (++sc.t == p.T) { sc.t = 0; ++sc.cc; }
-      if (grp < p.n_k) issue(sc, A);
-      for (int kit = grp; kit < p.n_k; kit += 2 * kGroups) {
+      if (grp < n_loc) issue(sc, A);
+      for (int kit = grp; kit < n_loc; kit += 2 * kGroups) {
         sc = next_coord(sc);
-        if (kit + kGroups < p.n_k) issue(sc, B);
+        if (kit + kGroups < n_loc) issue(sc, B);
         ok = consume(A);
-        if (!ok || kit + kGroups >= p.n_k) break;
+        if (!ok || kit + kGroups >= n_loc) break;
         sc = next_coord(sc);
-        if (kit + 2 * kGroups < p.n_k) issue(sc, A);
+        if (kit + 2 * kGroups < n_loc) issue(sc, A);
         ok = consume(B);
         if (!ok) break;
       }
@@ -522,17 +543,20 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   } else if (warp == R::kTma) {
     if (lane == 0) {
       int issued = 0;
-      for (int kit = 0; kit < p.n_k; ++kit) {
+      for (int kit = 0; kit < n_loc; ++kit) {
         const int s = kit % STAGES;
         const uint32_t ph = (kit / STAGES) & 1;
         if (!wait(bar_empty + 8 * s, ph ^ 1, kSiteTmaEmpty)) break;
-        const int t = kit % p.T;
-        const int cc = kit / p.T;
+        const int t = (N2 ? k_begin + kit : kit) % p.T;
+        const int cc = (N2 ? k_begin + kit : kit) / p.T;
         if constexpr (PAIR) {
           // the leader expects both CTAs' halves on its own barrier
           if (leader) ptx::mbar_arrive_expect_tx(bar_full + 8 * s, 2 * L::kBBytes);
-          ptx::tma_load_2d_pair(sB + s * L::kBBytes, &tmap_w, full_dst + 8 * s,
-                                t * p.Cin_pad + cc * kBK, n0 + static_cast<int>(cr) * L::kBRows);
+#pragma unroll
+          for (int h = 0; h < NH; ++h)
+            ptx::tma_load_2d_pair(sB + s * L::kBBytes + h * (BN / 2) * 128, &tmap_w,
+                                  full_dst + 8 * s, t * p.Cin_pad + cc * kBK,
+                                  n0 + h * BN + static_cast<int>(cr) * (BN / 2));
         } else {
           // NSPLIT: the other CTA's A rows land on the same barrier
           ptx::mbar_arrive_expect_tx(bar_full + 8 * s, L::kBBytes + (NSPLIT ? kGBytes : 0u));
@@ -553,7 +577,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   } else if (warp == R::kMma) {  // (the leader's, when paired)
     if (lane == 0 && (leader || !PAIR)) {
       constexpr uint32_t idesc = ptx::umma_idesc_f16(GM::kFmt, PAIR ? 2 * kBM : kBM, BN);
-      for (int kit = 0; kit < p.n_k; ++kit) {
+      for (int kit = 0; kit < n_loc; ++kit) {
         const int s = kit % STAGES;
         if (!wait(bar_full + 8 * s, (kit / STAGES) & 1, kSiteMmaFull)) break;
         ptx::tc_fence_after();
@@ -562,9 +586,14 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
 #pragma unroll
         for (int k = 0; k < kBK / 16; ++k) {
           const uint64_t ad = ptx::umma_desc_sw128(a_stage + k * 32);
-          const uint64_t bd = ptx::umma_desc_sw128(b_stage + k * 32);
-          if constexpr (PAIR) ptx::umma_f16_ss_pair(tmem_base, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
-          else ptx::umma_f16_ss(tmem_base, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {
+            // accumulator h: TMEM columns [h*BN, h*BN + BN), B half-tile h
+            const uint64_t bd = ptx::umma_desc_sw128(b_stage + h * (BN / 2) * 128 + k * 32);
+            if constexpr (PAIR)
+              ptx::umma_f16_ss_pair(tmem_base + h * BN, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
+            else ptx::umma_f16_ss(tmem_base, ad, bd, idesc, (kit | k) != 0 ? 1u : 0u);
+          }
         }
         if constexpr (PAIR) ptx::umma_commit_pair_both(bar_empty + 8 * s, 0x3);
         else if constexpr (NSPLIT) ptx::umma_commit_multicast(bar_empty + 8 * s, 0x3);
@@ -584,17 +613,104 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
 
   // ------------------------------------------------------------ epilogue
   // Warps 0-15 (gather, TMA, MMA and idle warps alike) drain TMEM: warp w
-  // reads lane quadrant w % 4, columns of quarter w / 4.
+  // reads lane quadrant w % 4, in windows of kColsPerWarp columns: window
+  // w / 4 of the tile's columns, or under kModePairN2 window w / 4 of each
+  // 256-column half (of the half this cluster finishes, when K is split).
   __syncwarp();
   if (warp < kEpilogueWarps) {
     if (ok) ok = wait(bar_tmem, 0, kSiteEpilogue);
+    constexpr int kColsPerWarp = N2 ? kSplitCols / 4 : NCOLS / 4;
+    constexpr int kChunk = kColsPerWarp < 32 ? kColsPerWarp : 32;
+    const int q = warp & 3;                        // TMEM lane quadrant of this warp
+    const int cgrp = warp >> 2;                    // its window in each column block
+    const int row = q * 32 + lane;
+    const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    int n_win = 1;
+    int win0 = cgrp * kColsPerWarp;
+    const float4 *partner = nullptr;               // K split: the other half's columns
+    if constexpr (N2) {
+      n_win = NCOLS / kSplitCols;
+      if (p.k_split > 1) {
+        // The cluster running K part k finishes columns [k*256, k*256+256) of
+        // the tile and hands the other 256 columns of its accumulator to the
+        // partner cluster: write them (fp32, [column/4][row][4], so a warp
+        // store covers 512 contiguous bytes), then meet the partner CTA on
+        // the (tile, rank) ticket.  Both clusters of a tile are resident at
+        // once (the host splits K only when all clusters fit on the GPU
+        // together), so the wait ends; it is bounded all the same.
+        const size_t slot = static_cast<size_t>(tile * 2 + static_cast<int>(cr)) * 2;
+        volatile int *s_met = reinterpret_cast<volatile int *>(smem + L::kMisc + 8);
+        if (ok) {
+          ptx::tc_fence_after();
+          const int give = (1 - k_part) * kSplitCols;
+          float4 *mine = reinterpret_cast<float4 *>(p.part) +
+                         (slot + k_part) * (kSplitCols / 4) * kBM + row;
+#pragma unroll 1
+          for (int cb = 0; cb < kColsPerWarp; cb += 32) {
+            const int c = cgrp * kColsPerWarp + cb;  // column within the handed-over half
+            uint32_t r[32];
+            ptx::tmem_ld_32x32b<32>(t_row + give + c, r);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              __stcg(mine + ((c >> 2) + g) * kBM,
+                     make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]),
+                                 __uint_as_float(r[4 * g + 2]), __uint_as_float(r[4 * g + 3])));
+          }
+          __threadfence();
+        }
+        ptx::named_barrier_sync(2, kEpilogueWarps * 32);
+        if (threadIdx.x == 0) {
+          // Rendezvous without a reset pass: both CTAs swap this launch's tag
+          // into the arrival word.  The one that gets the tag back arrives
+          // second (the other's partial sums are written) and releases the
+          // other through the second word; the first clears both words once
+          // released.  Words left by another launch or by unrelated data
+          // hold other values, so the workspace needs no initialisation; a
+          // replayed graph node keeps its grid id, and finds the words
+          // cleared by its previous run (a wait that gives up clears its
+          // arrival too).
+          int met = 0;
+          if (!*s_abort) {
+            unsigned long long *arrive = p.tickets + slot;        // (tile, rank): 2 words
+            unsigned long long *release = arrive + 1;
+            unsigned long long tag = (ptx::grid_id() + 1) * 0x9E3779B97F4A7C15ull;
+            tag = tag ? tag : 1ull;
+            if (ptx::atom_exch_acq_rel_gpu(arrive, tag) == tag) {
+              ptx::st_release_gpu(release, tag);
+              met = 1;
+            } else {
+              const uint64_t t0 = ptx::globaltimer_ns();
+              for (uint32_t it = 0;; ++it) {
+                if (ptx::ld_acquire_gpu(release) == tag) {
+                  *release = 0ull;
+                  *arrive = 0ull;
+                  met = 1;
+                  break;
+                }
+                __nanosleep(64);
+                if ((it & 7u) == 7u && ptx::globaltimer_ns() - t0 > p.wait_limit_ns) {
+                  ptx::atom_exch_acq_rel_gpu(arrive, 0ull);
+                  atomicCAS(&g_bevk_watchdog, 0u, static_cast<unsigned int>(kSiteSplitK));
+                  *s_abort = 1;
+                  break;
+                }
+              }
+            }
+          }
+          *s_met = met;
+        }
+        ptx::named_barrier_sync(2, kEpilogueWarps * 32);
+        if (!*s_met) ok = false;
+        __threadfence();
+        partner = reinterpret_cast<const float4 *>(p.part) +
+                  (slot + 1 - k_part) * (kSplitCols / 4) * kBM + row;
+        n_win = 1;
+        win0 = k_part * kSplitCols + cgrp * kColsPerWarp;
+      }
+    }
     if (ok) {
       ptx::tc_fence_after();
-      constexpr int kColsPerWarp = BN / 4;           // 4 warps share each TMEM lane quadrant
-      constexpr int kChunk = kColsPerWarp < 32 ? kColsPerWarp : 32;
-      const int q = warp & 3;                        // TMEM lane quadrant of this warp
-      const int cgrp = warp >> 2;                    // which quarter of the BN columns
-      const int row = q * 32 + lane;
       const int m = m0 + row;
       const int HoWo = p.Ho * p.Wo;
       const int b = m / HoWo, rem = m - (m / HoWo) * HoWo;
@@ -603,95 +719,115 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
       const bool vec_out = p.ys[1] == 1 && (p.Cout & 7) == 0 &&
                            (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (p.ys[0] & 7) == 0 &&
                            (p.ys[2] & 7) == 0 && (p.ys[3] & 7) == 0;
-      // A lane holds its own pixel's channels, so direct 16-byte stores put
-      // 32 pixels (32 lines) in every warp store.  When the warp's whole
-      // column range is in bounds and the output is channel-contiguous, its
-      // 32 x kColsPerWarp block is staged in shared memory and written back
-      // row by row, kColsPerWarp * 2 contiguous bytes per row.
-      if (vec_out && n0 + (cgrp + 1) * kColsPerWarp <= p.Cout) {
-        constexpr int kCh = kColsPerWarp / 8;          // 16-byte chunks a row
-        // Staged in the weight ring: only this CTA's TMA writes it and the
-        // MMAs (also the partner's, in a pair) have finished reading it.  The
-        // A ring is not free yet under N-split: bulk copies to the other CTA
-        // may still be reading it.
-        static_assert(kEpilogueWarps * 32 * kCh * 16 <= STAGES * L::kBBytes, "staging space");
-        const uint32_t blk = sB + static_cast<uint32_t>(warp * 32 * kCh * 16);
-#pragma unroll 1
-        for (int cb = 0; cb < kColsPerWarp; cb += kChunk) {
-          const int col = cgrp * kColsPerWarp + cb;
-          uint32_t r[kChunk];
-          ptx::tmem_ld_32x32b<kChunk>(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + col, r);
-          ptx::tmem_wait_ld();
-          const int co0 = n0 + col;
+      // accumulator columns [col, col + kChunk) of this lane's row (plus the
+      // partner half's partial sums under a K split)
+      auto acc = [&](int col, uint32_t(&r)[kChunk]) {
+        ptx::tmem_ld_32x32b<kChunk>(t_row + col, r);
+        ptx::tmem_wait_ld();
+        if (N2 && partner != nullptr) {
+          const float4 *pp = partner + ((col - k_part * kSplitCols) >> 2) * kBM;
 #pragma unroll
-          for (int g = 0; g < kChunk / 8; ++g) {
-            uint4 pk;
-            uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              float v0 = __uint_as_float(r[g * 8 + 2 * h]);
-              float v1 = __uint_as_float(r[g * 8 + 2 * h + 1]);
-              if (p.has_bias) {
-                v0 += ld_float(bias + co0 + g * 8 + 2 * h);
-                v1 += ld_float(bias + co0 + g * 8 + 2 * h + 1);
-              }
-              if (p.act_relu) {
-                v0 = fmaxf(v0, 0.f);
-                v1 = fmaxf(v1, 0.f);
-              }
-              pw[h] = static_cast<uint32_t>(GM::store_bits(v0)) |
-                      (static_cast<uint32_t>(GM::store_bits(v1)) << 16);
-            }
-            const int c = cb / 8 + g;
-            ptx::st_shared_v4(blk + lane * (kCh * 16) + ((c ^ (lane % kCh)) << 4), pk);
+          for (int g = 0; g < kChunk / 4; ++g) {
+            const float4 v = __ldcg(pp + g * kBM);
+            r[4 * g] = __float_as_uint(__uint_as_float(r[4 * g]) + v.x);
+            r[4 * g + 1] = __float_as_uint(__uint_as_float(r[4 * g + 1]) + v.y);
+            r[4 * g + 2] = __float_as_uint(__uint_as_float(r[4 * g + 2]) + v.z);
+            r[4 * g + 3] = __float_as_uint(__uint_as_float(r[4 * g + 3]) + v.w);
           }
         }
-        __syncwarp();
-        constexpr int kRowsPerStore = 32 / kCh;
-        const int c = lane % kCh;
-        const uint64_t yrow_bits = reinterpret_cast<uint64_t>(yrow);
-#pragma unroll
-        for (int i = 0; i < 32 / kRowsPerStore; ++i) {
-          const int rl = i * kRowsPerStore + lane / kCh;   // row of the warp's block
-          const uint4 v = ptx::ld_shared_v4(blk + rl * (kCh * 16) + ((c ^ (rl % kCh)) << 4));
-          T *yr = reinterpret_cast<T *>(__shfl_sync(0xffffffffu, yrow_bits, rl));
-          if (m0 + q * 32 + rl < p.M)
-            *reinterpret_cast<uint4 *>(yr + n0 + cgrp * kColsPerWarp + c * 8) = v;
-        }
-      } else {
+      };
 #pragma unroll 1
-        for (int cb = 0; cb < kColsPerWarp; cb += kChunk) {
-          const int col = cgrp * kColsPerWarp + cb;
-          if (n0 + col >= p.Cout) break;
-          uint32_t r[kChunk];
-          ptx::tmem_ld_32x32b<kChunk>(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + col, r);
-          ptx::tmem_wait_ld();
-          if (m < p.M) {
+      for (int wi = 0; wi < (N2 ? n_win : 1); ++wi) {
+        const int c0 = win0 + wi * kSplitCols;   // first tile column of the window
+        // A lane holds its own pixel's channels, so direct 16-byte stores put
+        // 32 pixels (32 lines) in every warp store.  When the window is in
+        // bounds and the output is channel-contiguous, the warp's 32 x
+        // kColsPerWarp block is staged in shared memory and written back row
+        // by row, kColsPerWarp * 2 contiguous bytes per row.
+        if (vec_out && n0 + c0 + kColsPerWarp <= p.Cout) {
+          constexpr int kCh = kColsPerWarp / 8;          // 16-byte chunks a row
+          // Staged in the weight ring: only this CTA's TMA writes it and the
+          // MMAs (also the partner's, in a pair) have finished reading it.  The
+          // A ring is not free yet under N-split: bulk copies to the other CTA
+          // may still be reading it.
+          static_assert(kEpilogueWarps * 32 * kCh * 16 <= STAGES * L::kBBytes, "staging space");
+          const uint32_t blk = sB + static_cast<uint32_t>(warp * 32 * kCh * 16);
+#pragma unroll 1
+          for (int cb = 0; cb < kColsPerWarp; cb += kChunk) {
+            const int col = c0 + cb;
+            uint32_t r[kChunk];
+            acc(col, r);
             const int co0 = n0 + col;
-            float v[kChunk];
 #pragma unroll
-            for (int jj = 0; jj < kChunk; ++jj) {
-              v[jj] = __uint_as_float(r[jj]);
-              if (p.has_bias && co0 + jj < p.Cout) v[jj] += ld_float(bias + co0 + jj);
-              if (p.act_relu) v[jj] = fmaxf(v[jj], 0.f);
-            }
-            if (vec_out && co0 + kChunk <= p.Cout) {
+            for (int g = 0; g < kChunk / 8; ++g) {
+              uint4 pk;
+              uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
 #pragma unroll
-              for (int g = 0; g < kChunk / 8; ++g) {
-                uint4 pk;
-                uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
-#pragma unroll
-                for (int h = 0; h < 4; ++h)
-                  pw[h] = static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h])) |
-                          (static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h + 1])) << 16);
-                *reinterpret_cast<uint4 *>(yrow + co0 + g * 8) = pk;
+              for (int h = 0; h < 4; ++h) {
+                float v0 = __uint_as_float(r[g * 8 + 2 * h]);
+                float v1 = __uint_as_float(r[g * 8 + 2 * h + 1]);
+                if (p.has_bias) {
+                  v0 += ld_float(bias + co0 + g * 8 + 2 * h);
+                  v1 += ld_float(bias + co0 + g * 8 + 2 * h + 1);
+                }
+                if (p.act_relu) {
+                  v0 = fmaxf(v0, 0.f);
+                  v1 = fmaxf(v1, 0.f);
+                }
+                pw[h] = static_cast<uint32_t>(GM::store_bits(v0)) |
+                        (static_cast<uint32_t>(GM::store_bits(v1)) << 16);
               }
-            } else {
+              const int c = cb / 8 + g;
+              ptx::st_shared_v4(blk + lane * (kCh * 16) + ((c ^ (lane % kCh)) << 4), pk);
+            }
+          }
+          __syncwarp();
+          constexpr int kRowsPerStore = 32 / kCh;
+          const int c = lane % kCh;
+          const uint64_t yrow_bits = reinterpret_cast<uint64_t>(yrow);
+#pragma unroll
+          for (int i = 0; i < 32 / kRowsPerStore; ++i) {
+            const int rl = i * kRowsPerStore + lane / kCh;   // row of the warp's block
+            const uint4 v = ptx::ld_shared_v4(blk + rl * (kCh * 16) + ((c ^ (rl % kCh)) << 4));
+            T *yr = reinterpret_cast<T *>(__shfl_sync(0xffffffffu, yrow_bits, rl));
+            if (m0 + q * 32 + rl < p.M)
+              *reinterpret_cast<uint4 *>(yr + n0 + c0 + c * 8) = v;
+          }
+          __syncwarp();   // the block is rewritten by the next window
+        } else {
+#pragma unroll 1
+          for (int cb = 0; cb < kColsPerWarp; cb += kChunk) {
+            const int col = c0 + cb;
+            if (n0 + col >= p.Cout) break;
+            uint32_t r[kChunk];
+            acc(col, r);
+            if (m < p.M) {
+              const int co0 = n0 + col;
+              float v[kChunk];
 #pragma unroll
               for (int jj = 0; jj < kChunk; ++jj) {
-                if (co0 + jj < p.Cout) {
-                  const uint16_t bits = GM::store_bits(v[jj]);
-                  *reinterpret_cast<uint16_t *>(yrow + (co0 + jj) * p.ys[1]) = bits;
+                v[jj] = __uint_as_float(r[jj]);
+                if (p.has_bias && co0 + jj < p.Cout) v[jj] += ld_float(bias + co0 + jj);
+                if (p.act_relu) v[jj] = fmaxf(v[jj], 0.f);
+              }
+              if (vec_out && co0 + kChunk <= p.Cout) {
+#pragma unroll
+                for (int g = 0; g < kChunk / 8; ++g) {
+                  uint4 pk;
+                  uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
+#pragma unroll
+                  for (int h = 0; h < 4; ++h)
+                    pw[h] = static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h])) |
+                            (static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h + 1])) << 16);
+                  *reinterpret_cast<uint4 *>(yrow + co0 + g * 8) = pk;
+                }
+              } else {
+#pragma unroll
+                for (int jj = 0; jj < kChunk; ++jj) {
+                  if (co0 + jj < p.Cout) {
+                    const uint16_t bits = GM::store_bits(v[jj]);
+                    *reinterpret_cast<uint16_t *>(yrow + (co0 + jj) * p.ys[1]) = bits;
+                  }
                 }
               }
             }
@@ -708,7 +844,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   if constexpr (CLUSTER) ptx::cluster_sync();
   if (warp == R::kMma) {
     ptx::tc_fence_after();
-    if constexpr (PAIR) ptx::tmem_dealloc_pair(tmem_base, BN);
+    if constexpr (PAIR) ptx::tmem_dealloc_pair(tmem_base, NCOLS);
     else ptx::tmem_dealloc(tmem_base, BN);
   }
 }
@@ -729,6 +865,15 @@ dcn_fwd_tc_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParam
                        const T *__restrict__ msk, const T *__restrict__ bias,
                        T *__restrict__ y) {
   dcn_fwd_tc_body<T, BN, STAGES, kModePair, VB>(tmap_w, p, x, off, msk, bias, y);
+}
+
+template <typename T, int BN, int STAGES, int VB>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc_threads<kModePairN2>(), 1)
+dcn_fwd_tc_pairn2_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcParams p,
+                         const T *__restrict__ x, const T *__restrict__ off,
+                         const T *__restrict__ msk, const T *__restrict__ bias,
+                         T *__restrict__ y) {
+  dcn_fwd_tc_body<T, BN, STAGES, kModePairN2, VB>(tmap_w, p, x, off, msk, bias, y);
 }
 
 template <typename T, int BN, int STAGES, int VB>
@@ -769,10 +914,12 @@ struct TypeTag {
 template <typename T, int BN, int STAGES, int MODE, int VB>
 int launch_tc(const TcParams &p, const CUtensorMap &tmap, const void *x, const void *off,
               const void *msk, const void *bias, void *y, int ctas, cudaStream_t stream) {
-  using L = Smem<BN, STAGES, MODE == kModePair>;
+  using L = Smem<BN, STAGES, MODE == kModePair || MODE == kModePairN2,
+                 MODE == kModePairN2 ? 2 : 1>;
   static_assert(L::kAlloc <= 232448, "shared memory budget");
   auto kern = [] {
     if constexpr (MODE == kModePair) return dcn_fwd_tc_pair_kernel<T, BN, STAGES, VB>;
+    else if constexpr (MODE == kModePairN2) return dcn_fwd_tc_pairn2_kernel<T, BN, STAGES, VB>;
     else if constexpr (MODE == kModeNSplit) return dcn_fwd_tc_nsplit_kernel<T, BN, STAGES, VB>;
     else return dcn_fwd_tc_kernel<T, BN, STAGES, VB>;
   }();
@@ -789,6 +936,27 @@ int launch_tc(const TcParams &p, const CUtensorMap &tmap, const void *x, const v
   if (attr_err[dev] != cudaSuccess)
     return fail(BEVK_ERR_CUDA, "dcn tc: cudaFuncSetAttribute: %s",
                 cudaGetErrorString(attr_err[dev]));
+  if constexpr (MODE == kModePairN2) {
+    if (p.k_split > 1) {
+      // The two K parts of a tile wait for each other: every cluster must be
+      // resident at once, or the caller takes a schedule without the split.
+      static std::once_flag occ_once[kMaxDevices];
+      static int max_clusters[kMaxDevices];
+      std::call_once(occ_once[dev], [&] {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2);
+        cfg.blockDim = dim3(tc_threads<MODE>());
+        cfg.dynamicSmemBytes = L::kAlloc;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+          (void)cudaGetLastError();
+          n = 0;
+        }
+        max_clusters[dev] = n;
+      });
+      if (ctas / 2 > max_clusters[dev]) return BEVK_ERR_UNSUPPORTED;
+    }
+  }
   // Programmatic dependent launch: the kernel's prologue overlaps the tail of
   // the stream's previous kernel; it waits for that kernel (griddepcontrol)
   // before touching global memory.
@@ -812,9 +980,59 @@ bool dcn_tc_supported(const bevk_dcn_problem *pr, const DcnDims &d) {
   return true;
 }
 
+namespace {
+constexpr int kMinSplitStages = 8;   // K stages of each part, at least
+
+// Tiles of the two-accumulator schedule with its K split in two, or 0 when
+// the problem does not take it: more than 256 output channels, and all four
+// CTAs of every 256-pixel x 512-channel tile fit on the SMs at once (the
+// problems whose N-split grid fills at most one wave; per tile and stage the
+// paired M=256 MMAs into two accumulators do the work of two N-split stages
+// in about 1.5 times the time).
+int64_t n2_split_tiles(const DcnDims &d) {
+  if (d.Cout <= 256) return 0;
+  const int n_k = d.T * (d.Cin_g_pad / kBK);
+  if (n_k < 2 * kMinSplitStages) return 0;
+  const int64_t tiles = ((d.M + 2 * kBM - 1) / (2 * kBM)) * ((d.Cout + 511) / 512);
+  const int sms = device_info(current_device()).sm_count;
+  if (sms <= 0 || 4 * tiles > sms) return 0;
+  return tiles;
+}
+
+size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+
+// K-split scratch: tickets [tile][rank][2] (uint64), then the handed-over
+// accumulator halves [tile][rank][K part][kSplitCols / 4][kBM][4] (fp32).
+size_t split_tickets_bytes(int64_t tiles) {
+  return align256(static_cast<size_t>(tiles) * 2 * 2 * sizeof(unsigned long long));
+}
+size_t split_ws_bytes(int64_t tiles) {
+  return split_tickets_bytes(tiles) +
+         static_cast<size_t>(tiles) * 4 * kSplitCols * kBM * sizeof(float);
+}
+
+// Schedule-dependent fields of p; returns the number of CTAs.
+int64_t set_schedule(TcParams &p, const DcnDims &d, int mode, int BN, int k_split) {
+  const int tile_n = mode == kModeNSplit || mode == kModePairN2 ? 2 * BN : BN;
+  p.n_tiles_n = (d.Cout + tile_n - 1) / tile_n;
+  p.k_split = k_split;
+  p.k_len = (p.n_k + k_split - 1) / k_split;
+  const bool pair = mode == kModePair || mode == kModePairN2;
+  const int64_t m_tiles = pair ? (d.M + 2 * kBM - 1) / (2 * kBM) : (d.M + kBM - 1) / kBM;
+  return (mode == kModeSingle ? 1 : 2) * m_tiles * p.n_tiles_n * k_split;
+}
+}  // namespace
+
+size_t dcn_tc_workspace_bytes(const bevk_dcn_problem *p, const DcnDims &d) {
+  if (!dcn_tc_supported(p, d)) return 0;
+  const int64_t tiles = n2_split_tiles(d);
+  return tiles ? split_ws_bytes(tiles) : 0;
+}
+
 int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const void *x,
                           const int64_t xs[4], const void *off, const void *msk,
-                          const void *wpk, const void *bias, void *y, cudaStream_t stream) {
+                          const void *wpk, const void *bias, void *y, void *ws, size_t ws_bytes,
+                          cudaStream_t stream) {
   if (xs[1] != 1 || xs[0] % 8 || xs[2] % 8 || xs[3] % 8 || !aligned(x, 16) || !aligned(wpk, 16))
     return fail(BEVK_ERR_MISALIGNED, "dcn tc: input must be channel-contiguous with 16-byte rows");
   const int64_t extent = (d.B - 1) * xs[0] + (d.H - 1) * xs[2] + (d.W - 1) * xs[3] + d.Cin;
@@ -833,12 +1051,20 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
   p.Cin_pad = d.Cin_g_pad;
   p.n_cc = p.Cin_pad / kBK;
   p.n_k = p.T * p.n_cc;
-  // Tile schedule: more than 256 output channels -> N-split CTA pairs (one
-  // gather per pixel for 512 channels); 129..256 -> M-paired CTAs (M=256
-  // MMA, half the weight tile per CTA); up to 128 -> single CTAs.
-  const int mode = d.Cout > 256 ? kModeNSplit : (BN == 256 ? kModePair : kModeSingle);
-  p.n_tiles_n = (d.Cout + (mode == kModeNSplit ? 2 * BN : BN) - 1) /
-                (mode == kModeNSplit ? 2 * BN : BN);
+  p.part = nullptr;
+  p.tickets = nullptr;
+  // Tile schedule: more than 256 output channels -> paired M=256 CTAs with
+  // two accumulators and K split in two when the problem fills at most one
+  // wave and scratch is given, else N-split CTA pairs (one gather per pixel
+  // for 512 channels); 129..256 -> M-paired CTAs (M=256 MMA, half the weight
+  // tile per CTA); up to 128 -> single CTAs.
+  int mode = d.Cout > 256 ? kModeNSplit : (BN == 256 ? kModePair : kModeSingle);
+  const int64_t split_tiles = n2_split_tiles(d);
+  if (split_tiles && ws && aligned(ws, 256) && ws_bytes >= split_ws_bytes(split_tiles)) {
+    mode = kModePairN2;
+    p.tickets = static_cast<unsigned long long *>(ws);
+    p.part = reinterpret_cast<float *>(static_cast<char *>(ws) + split_tickets_bytes(split_tiles));
+  }
   p.mask_is_logit = pr->mask_is_logit;
   p.has_bias = pr->has_bias;
   p.act_relu = pr->act_relu;
@@ -849,26 +1075,29 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
     p.ms[i] = pr->mask_strides[i];
     p.ys[i] = pr->output_strides[i];
   }
-  const bool pair = mode == kModePair;
-  const int64_t ctas = pair ? 2 * ((d.M + 2 * kBM - 1) / (2 * kBM)) * p.n_tiles_n
-                            : (mode == kModeNSplit ? 2 : 1) * ((d.M + kBM - 1) / kBM) * p.n_tiles_n;
+  const int64_t ctas = set_schedule(p, d, mode, BN, mode == kModePairN2 ? 2 : 1);
   if (ctas > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "dcn tc: too many tiles");
 
+  // A paired CTA loads its half of each BN-channel weight tile per stage.
+  auto make_map = [&](bool pair, CUtensorMap *tmap) -> int {
+    const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(d.T) * p.Cin_pad,
+                                static_cast<cuuint64_t>(d.Cout)};
+    const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(d.T) * p.Cin_pad * 2};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK),
+                               static_cast<cuuint32_t>(pair ? BN / 2 : BN)};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUtensorMapDataType dt = pr->dtype == BEVK_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const CUresult cr = enc(tmap, dt, 2, const_cast<void *>(wpk), gdim, gstride, box, estride,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return fail(BEVK_ERR_CUDA, "dcn tc: tensor map encode failed (%d)", int(cr));
+    return BEVK_OK;
+  };
   CUtensorMap tmap;
-  const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(d.T) * p.Cin_pad,
-                              static_cast<cuuint64_t>(d.Cout)};
-  const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(d.T) * p.Cin_pad * 2};
-  // A paired CTA loads its half of the BN output channels per stage.
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(pair ? BN / 2 : BN)};
-  const cuuint32_t estride[2] = {1, 1};
-  const CUtensorMapDataType dt = pr->dtype == BEVK_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  const CUresult cr = enc(&tmap, dt, 2, const_cast<void *>(wpk), gdim, gstride, box, estride,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) return fail(BEVK_ERR_CUDA, "dcn tc: tensor map encode failed (%d)", int(cr));
+  int st = make_map(mode == kModePair || mode == kModePairN2, &tmap);
+  if (st != BEVK_OK) return st;
 
-  const int nc = static_cast<int>(ctas);
   // 32-byte corner loads when every pixel row starts on a 32-byte boundary
   // and a lane's 16 channels are all inside or all outside Cin (N-split CTAs
   // gather 64 rows: one 16-byte vector per lane covers them).
@@ -876,6 +1105,17 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
                    xs[2] % 16 == 0 && xs[3] % 16 == 0 && aligned(x, 32);
   auto go = [&](auto tag) -> int {
     using T = typename decltype(tag)::type;
+    int nc = static_cast<int>(ctas);
+    if (mode == kModePairN2) {
+      // BEVK_ERR_UNSUPPORTED: the clusters would not all be resident at once
+      const int rc = v32 ? launch_tc<T, 256, 3, kModePairN2, 32>(p, tmap, x, off, msk, bias, y, nc, stream)
+                         : launch_tc<T, 256, 3, kModePairN2, 16>(p, tmap, x, off, msk, bias, y, nc, stream);
+      if (rc != BEVK_ERR_UNSUPPORTED) return rc;
+      mode = kModeNSplit;
+      nc = static_cast<int>(set_schedule(p, d, mode, BN, 1));
+      const int mst = make_map(false, &tmap);
+      if (mst != BEVK_OK) return mst;
+    }
     // N-split CTAs hold the whole 256-channel weight tile per stage: three
     // stages keep shared memory at 159 KB, leaving ~92 KB of L1 for the
     // corner reads (four stages would leave ~28 KB and halve the hit rate).

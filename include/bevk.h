@@ -139,7 +139,14 @@ BEVK_API size_t bevk_dcn_packed_weight_bytes(const bevk_dcn_problem *p);
 BEVK_API int bevk_dcn_pack_weight(const bevk_dcn_problem *p, const void *weight,
                                   void *packed_weight, bevk_stream_t stream);
 
-/* Scratch bytes bevk_dcn_forward needs for this problem (0 when none). */
+/*
+ * Scratch bytes for bevk_dcn_forward on this problem (0 when none): an NHWC
+ * copy of an input that is not channel-contiguous (required), followed by the
+ * tensor-core kernel's K-split scratch (optional: problems with more than 256
+ * output channels that fill at most one wave of the GPU split their K loop in
+ * two when it is given; with less workspace they run unsplit).  256-byte
+ * aligned workspace; its contents need no initialisation.
+ */
 BEVK_API size_t bevk_dcn_forward_workspace_bytes(const bevk_dcn_problem *p);
 
 /*

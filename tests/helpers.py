@@ -60,12 +60,15 @@ def problem(x, off, mask, out, Cout, k, stride, pad, dil, groups=1, dg=1, mask_i
 
 
 def cabi_dcn_forward(x, off, mask, w, b, out, stride, pad, dil, groups=1, dg=1,
-                     mask_is_logit=False):
-    """Pack + forward through the C ABI (ctypes) on the current stream."""
+                     mask_is_logit=False, workspace=True, act_relu=False):
+    """Pack + forward through the C ABI (ctypes) on the current stream.
+    workspace=False passes no workspace (valid for channel-contiguous input:
+    the kernel then takes a schedule without K split)."""
     L = cabi.lib()
     k = (w.shape[2], w.shape[3])
     p = problem(x, off, mask, out, w.shape[0], k, stride, pad, dil, groups, dg, mask_is_logit,
                 b is not None)
+    p.act_relu = int(act_relu)
     stream = torch.cuda.current_stream().cuda_stream
     nbytes = L.bevk_dcn_packed_weight_bytes(ctypes.byref(p))
     assert nbytes > 0, cabi.last_error()
@@ -73,7 +76,7 @@ def cabi_dcn_forward(x, off, mask, w, b, out, stride, pad, dil, groups=1, dg=1,
     wc = w.contiguous()
     cabi.check(L.bevk_dcn_pack_weight(ctypes.byref(p), wc.data_ptr(), wpk.data_ptr(), stream),
                "pack")
-    ws_bytes = L.bevk_dcn_forward_workspace_bytes(ctypes.byref(p))
+    ws_bytes = L.bevk_dcn_forward_workspace_bytes(ctypes.byref(p)) if workspace else 0
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
     cabi.check(L.bevk_dcn_forward(ctypes.byref(p), x.data_ptr(), off.data_ptr(), mask.data_ptr(),
                                   wpk.data_ptr(), b.data_ptr() if b is not None else None,
