@@ -110,6 +110,9 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
 __device__ __forceinline__ unsigned long long grid_id() {
   unsigned long long g;
   asm volatile("mov.u64 %0, %%gridid;" : "=l"(g));

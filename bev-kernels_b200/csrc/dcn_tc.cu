@@ -72,6 +72,7 @@ enum : unsigned int {
 struct TcParams {
   int Cin, H, W, Ho, Wo, Cout, kW, T;
   int sh, sw, ph, pw, dh, dw;
+  int tap_dy[kMaxTaps], tap_dx[kMaxTaps];   // ki * dh - ph, kj * dw - pw of tap t
   int M, Cin_pad, n_cc, n_k, n_tiles_n;
   int mask_is_logit, has_bias, act_relu;
   int xs0, xs2, xs3;        // input strides (channel stride is 1)
@@ -190,6 +191,11 @@ struct GatherMath<__half> {
     __half h = __float2half_rn(v);
     return *reinterpret_cast<uint16_t *>(&h);
   }
+  // (lo, hi) rounded to the output type, lo in the low half
+  __device__ static uint32_t pack2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+  }
 };
 
 // bf16: weights as bf16x2 (w, w); packed bf16x2 FMA chain, each step
@@ -216,6 +222,10 @@ struct GatherMath<__nv_bfloat16> {
     __nv_bfloat16 h = __float2bfloat16_rn(v);
     return *reinterpret_cast<uint16_t *>(&h);
   }
+  __device__ static uint32_t pack2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+  }
 };
 
 template <typename T>
@@ -227,31 +237,21 @@ __device__ __forceinline__ float ld_float<__nv_bfloat16>(const __nv_bfloat16 *p)
   return __bfloat162float(*p);
 }
 
-// Geometry of (tile row r, tap t).  `packed` = 2 * (element offset of corner
-// (h_low, w_low)) | (in-range bits of corners 0..3); the offset is a multiple
-// of 8 elements, so the low four bits are free and the offset comes back as
-// (packed >> 1) & ~7.  `wh` = the four corner weights (mask folded in, 0 for
-// dropped corners) as 16-bit values of type T.
+// Geometry of output pixel m = (b, oh, ow) at tap t: `packed` = 2 * (element
+// offset of corner (h_low, w_low)) | (in-range bits of corners 0..3) -- the
+// offset is a multiple of 8 elements, so the low four bits are free and the
+// offset comes back as (packed >> 1) & ~7 -- and `wh` = the four corner
+// weights (mask folded in, 0 for dropped corners) as 16-bit values of type T.
+// (dy, dx, mk) are the pixel's offsets and mask at tap t.
 template <typename T>
-__device__ __forceinline__ void tap_geometry(const TcParams &p, const T *__restrict__ off,
-                                             const T *__restrict__ msk, int m, int t,
-                                             int &packed, uint2 &wh) {
+__device__ __forceinline__ void tap_geometry(const TcParams &p, int b, int oh, int ow, int t,
+                                             float dy, float dx, float mk, int &packed,
+                                             uint2 &wh) {
   packed = 0;
   wh = make_uint2(0u, 0u);
-  if (m >= p.M) return;
-  const int HoWo = p.Ho * p.Wo;
-  const int b = m / HoWo;
-  const int rem = m - b * HoWo;
-  const int oh = rem / p.Wo;
-  const int ow = rem - oh * p.Wo;
-  const int ki = t / p.kW, kj = t - (t / p.kW) * p.kW;
-  const T *ob = off + b * p.os[0] + oh * p.os[2] + ow * p.os[3];
-  const float off_h = ld_float(ob + (2 * t) * p.os[1]);
-  const float off_w = ld_float(ob + (2 * t + 1) * p.os[1]);
-  float mk = ld_float(msk + b * p.ms[0] + t * p.ms[1] + oh * p.ms[2] + ow * p.ms[3]);
   if (p.mask_is_logit) mk = 1.f / (1.f + __expf(-mk));
-  const float h_im = static_cast<float>(oh * p.sh - p.ph + ki * p.dh) + off_h;
-  const float w_im = static_cast<float>(ow * p.sw - p.pw + kj * p.dw) + off_w;
+  const float h_im = static_cast<float>(oh * p.sh + p.tap_dy[t]) + dy;
+  const float w_im = static_cast<float>(ow * p.sw + p.tap_dx[t]) + dx;
   if (!(h_im > -1.f && w_im > -1.f && h_im < static_cast<float>(p.H) &&
         w_im < static_cast<float>(p.W)))
     return;
@@ -387,13 +387,49 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
   bool ok = true;
   if (gather_warp) {
     // ---------------------------------------------------------- geometry
-    for (int e = gw * 32 + lane; e < p.T * kGRows; e += kGatherWarps * 32) {
-      const int t = e / kGRows, r = e - (e / kGRows) * kGRows;
-      int packed;
-      uint2 wh;
-      tap_geometry<T>(p, off, msk, m0 + g_row0 + r, t, packed, wh);
-      s_gb[e] = packed;
-      s_gw[e] = wh;
+    // Entry e = t * kGRows + r for every tap t and tile row r.  A thread owns
+    // one row (its pixel decoded once) and every kPerRow-th tap of it; the
+    // lanes of a warp take consecutive rows, so each offset / mask load of a
+    // warp is one contiguous run.  All of a thread's loads are issued before
+    // any entry is computed.
+    {
+      constexpr int kPerRow = kGatherWarps * 32 / kGRows;
+      constexpr int kMaxPer = (kMaxTaps + kPerRow - 1) / kPerRow;
+      const int j = gw * 32 + lane;
+      const int r = j % kGRows, t0 = j / kGRows;
+      const int m = m0 + g_row0 + r;
+      int b = 0, oh = 0, ow = 0;
+      if (m < p.M) {
+        const int HoWo = p.Ho * p.Wo;
+        b = m / HoWo;
+        const int rem = m - b * HoWo;
+        oh = rem / p.Wo;
+        ow = rem - oh * p.Wo;
+      }
+      const T *ob = off + b * p.os[0] + oh * p.os[2] + ow * p.os[3];
+      const T *mb = msk + b * p.ms[0] + oh * p.ms[2] + ow * p.ms[3];
+      float dy[kMaxPer], dx[kMaxPer], mk[kMaxPer];
+#pragma unroll
+      for (int i = 0; i < kMaxPer; ++i) {
+        const int t = t0 + i * kPerRow;
+        dy[i] = dx[i] = mk[i] = 0.f;
+        if (t < p.T && m < p.M) {
+          dy[i] = ld_float(ob + (2 * t) * p.os[1]);
+          dx[i] = ld_float(ob + (2 * t + 1) * p.os[1]);
+          mk[i] = ld_float(mb + t * p.ms[1]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kMaxPer; ++i) {
+        const int t = t0 + i * kPerRow;
+        if (t < p.T) {
+          int packed = 0;
+          uint2 wh = make_uint2(0u, 0u);
+          if (m < p.M) tap_geometry<T>(p, b, oh, ow, t, dy[i], dx[i], mk[i], packed, wh);
+          s_gb[t * kGRows + r] = packed;
+          s_gw[t * kGRows + r] = wh;
+        }
+      }
     }
     ptx::named_barrier_sync(1, kGatherWarps * 32);
 
@@ -707,6 +743,12 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
                   (slot + 1 - k_part) * (kSplitCols / 4) * kBM + row;
         n_win = 1;
         win0 = k_part * kSplitCols + cgrp * kColsPerWarp;
+        if (ok) {
+          // all of this lane's partner sums in flight at once, into L1
+          const float4 *pp = partner + (cgrp * kColsPerWarp >> 2) * kBM;
+#pragma unroll
+          for (int g = 0; g < kColsPerWarp / 4; ++g) ptx::prefetch_l1(pp + g * kBM);
+        }
       }
     }
     if (ok) {
@@ -721,20 +763,32 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
                            (p.ys[2] & 7) == 0 && (p.ys[3] & 7) == 0;
       // accumulator columns [col, col + kChunk) of this lane's row (plus the
       // partner half's partial sums under a K split)
+      auto add_partner = [&](int col, uint32_t(&r)[kChunk]) {
+        if (N2 && partner != nullptr) {
+          const float4 *pp = partner + ((col - k_part * kSplitCols) >> 2) * kBM;
+          // four loads (16 registers) in flight at a time: the accumulator
+          // chunks already hold 64
+#pragma unroll
+          for (int g0 = 0; g0 < kChunk / 4; g0 += 4) {
+            float4 v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = __ldca(pp + (g0 + i) * kBM);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int g = g0 + i;
+              r[4 * g] = __float_as_uint(__uint_as_float(r[4 * g]) + v[i].x);
+              r[4 * g + 1] = __float_as_uint(__uint_as_float(r[4 * g + 1]) + v[i].y);
+              r[4 * g + 2] = __float_as_uint(__uint_as_float(r[4 * g + 2]) + v[i].z);
+              r[4 * g + 3] = __float_as_uint(__uint_as_float(r[4 * g + 3]) + v[i].w);
+            }
+            asm volatile("" ::: "memory");
+          }
+        }
+      };
       auto acc = [&](int col, uint32_t(&r)[kChunk]) {
         ptx::tmem_ld_32x32b<kChunk>(t_row + col, r);
         ptx::tmem_wait_ld();
-        if (N2 && partner != nullptr) {
-          const float4 *pp = partner + ((col - k_part * kSplitCols) >> 2) * kBM;
-#pragma unroll
-          for (int g = 0; g < kChunk / 4; ++g) {
-            const float4 v = __ldcg(pp + g * kBM);
-            r[4 * g] = __float_as_uint(__uint_as_float(r[4 * g]) + v.x);
-            r[4 * g + 1] = __float_as_uint(__uint_as_float(r[4 * g + 1]) + v.y);
-            r[4 * g + 2] = __float_as_uint(__uint_as_float(r[4 * g + 2]) + v.z);
-            r[4 * g + 3] = __float_as_uint(__uint_as_float(r[4 * g + 3]) + v.w);
-          }
-        }
+        add_partner(col, r);
       };
 #pragma unroll 1
       for (int wi = 0; wi < (N2 ? n_win : 1); ++wi) {
@@ -752,20 +806,30 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
           // may still be reading it.
           static_assert(kEpilogueWarps * 32 * kCh * 16 <= STAGES * L::kBBytes, "staging space");
           const uint32_t blk = sB + static_cast<uint32_t>(warp * 32 * kCh * 16);
-#pragma unroll 1
-          for (int cb = 0; cb < kColsPerWarp; cb += kChunk) {
-            const int col = c0 + cb;
-            uint32_t r[kChunk];
-            acc(col, r);
-            const int co0 = n0 + col;
+          // Every chunk's TMEM load in flight before the first wait; under
+          // the K split one chunk at a time (the partner's sums need the
+          // registers).
+          constexpr int kNChunks = kColsPerWarp / kChunk;
+          constexpr int kBatch = N2 ? 1 : kNChunks;
+          uint32_t r[kNChunks][kChunk];
+#pragma unroll
+          for (int cc = 0; cc < kNChunks; ++cc) {
+            if (cc % kBatch == 0) {
+#pragma unroll
+              for (int c2 = cc; c2 < cc + kBatch; ++c2)
+                ptx::tmem_ld_32x32b<kChunk>(t_row + c0 + c2 * kChunk, r[c2]);
+              ptx::tmem_wait_ld();
+            }
+            add_partner(c0 + cc * kChunk, r[cc]);
+            const int co0 = n0 + c0 + cc * kChunk;
 #pragma unroll
             for (int g = 0; g < kChunk / 8; ++g) {
               uint4 pk;
               uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
 #pragma unroll
               for (int h = 0; h < 4; ++h) {
-                float v0 = __uint_as_float(r[g * 8 + 2 * h]);
-                float v1 = __uint_as_float(r[g * 8 + 2 * h + 1]);
+                float v0 = __uint_as_float(r[cc][g * 8 + 2 * h]);
+                float v1 = __uint_as_float(r[cc][g * 8 + 2 * h + 1]);
                 if (p.has_bias) {
                   v0 += ld_float(bias + co0 + g * 8 + 2 * h);
                   v1 += ld_float(bias + co0 + g * 8 + 2 * h + 1);
@@ -774,10 +838,9 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
                   v0 = fmaxf(v0, 0.f);
                   v1 = fmaxf(v1, 0.f);
                 }
-                pw[h] = static_cast<uint32_t>(GM::store_bits(v0)) |
-                        (static_cast<uint32_t>(GM::store_bits(v1)) << 16);
+                pw[h] = GM::pack2(v0, v1);
               }
-              const int c = cb / 8 + g;
+              const int c = cc * (kChunk / 8) + g;
               ptx::st_shared_v4(blk + lane * (kCh * 16) + ((c ^ (lane % kCh)) << 4), pk);
             }
           }
@@ -816,9 +879,7 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
                   uint4 pk;
                   uint32_t *pw = reinterpret_cast<uint32_t *>(&pk);
 #pragma unroll
-                  for (int h = 0; h < 4; ++h)
-                    pw[h] = static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h])) |
-                            (static_cast<uint32_t>(GM::store_bits(v[g * 8 + 2 * h + 1])) << 16);
+                  for (int h = 0; h < 4; ++h) pw[h] = GM::pack2(v[g * 8 + 2 * h], v[g * 8 + 2 * h + 1]);
                   *reinterpret_cast<uint4 *>(yrow + co0 + g * 8) = pk;
                 }
               } else {
@@ -1047,6 +1108,10 @@ int launch_dcn_forward_tc(const bevk_dcn_problem *pr, const DcnDims &d, const vo
   p.Cin = d.Cin; p.H = d.H; p.W = d.W; p.Ho = d.Ho; p.Wo = d.Wo; p.Cout = d.Cout;
   p.kW = d.kW; p.T = d.T;
   p.sh = d.sh; p.sw = d.sw; p.ph = d.ph; p.pw = d.pw; p.dh = d.dh; p.dw = d.dw;
+  for (int t = 0; t < kMaxTaps; ++t) {
+    p.tap_dy[t] = t < d.T ? (t / d.kW) * d.dh - d.ph : 0;
+    p.tap_dx[t] = t < d.T ? (t % d.kW) * d.dw - d.pw : 0;
+  }
   p.M = static_cast<int>(d.M);
   p.Cin_pad = d.Cin_g_pad;
   p.n_cc = p.Cin_pad / kBK;
