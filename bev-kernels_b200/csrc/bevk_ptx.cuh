@@ -110,6 +110,13 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// 16-bit read-only load, issued where it stands (volatile: the compiler keeps
+// a batch of them ahead of the code that uses the values).
+__device__ __forceinline__ uint16_t ld_global_nc_u16(const void *p) {
+  uint16_t v;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
 __device__ __forceinline__ void prefetch_l1(const void *p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }

@@ -196,6 +196,7 @@ struct GatherMath<__half> {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&h);
   }
+  __device__ static float from_bits(uint16_t v) { return __half2float(__ushort_as_half(v)); }
 };
 
 // bf16: weights as bf16x2 (w, w); packed bf16x2 FMA chain, each step
@@ -225,6 +226,9 @@ struct GatherMath<__nv_bfloat16> {
   __device__ static uint32_t pack2(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&h);
+  }
+  __device__ static float from_bits(uint16_t v) {
+    return __uint_as_float(static_cast<uint32_t>(v) << 16);
   }
 };
 
@@ -406,18 +410,16 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
         oh = rem / p.Wo;
         ow = rem - oh * p.Wo;
       }
+      // (entries past the last tap or pixel load element 0 and are dropped)
       const T *ob = off + b * p.os[0] + oh * p.os[2] + ow * p.os[3];
       const T *mb = msk + b * p.ms[0] + oh * p.ms[2] + ow * p.ms[3];
-      float dy[kMaxPer], dx[kMaxPer], mk[kMaxPer];
+      uint16_t dy[kMaxPer], dx[kMaxPer], mk[kMaxPer];
 #pragma unroll
       for (int i = 0; i < kMaxPer; ++i) {
-        const int t = t0 + i * kPerRow;
-        dy[i] = dx[i] = mk[i] = 0.f;
-        if (t < p.T && m < p.M) {
-          dy[i] = ld_float(ob + (2 * t) * p.os[1]);
-          dx[i] = ld_float(ob + (2 * t + 1) * p.os[1]);
-          mk[i] = ld_float(mb + t * p.ms[1]);
-        }
+        const int t = t0 + i * kPerRow < p.T ? t0 + i * kPerRow : 0;
+        dy[i] = ptx::ld_global_nc_u16(ob + (2 * t) * p.os[1]);
+        dx[i] = ptx::ld_global_nc_u16(ob + (2 * t + 1) * p.os[1]);
+        mk[i] = ptx::ld_global_nc_u16(mb + t * p.ms[1]);
       }
 #pragma unroll
       for (int i = 0; i < kMaxPer; ++i) {
@@ -425,7 +427,9 @@ __device__ __forceinline__ void dcn_fwd_tc_body(const CUtensorMap &tmap_w, const
         if (t < p.T) {
           int packed = 0;
           uint2 wh = make_uint2(0u, 0u);
-          if (m < p.M) tap_geometry<T>(p, b, oh, ow, t, dy[i], dx[i], mk[i], packed, wh);
+          if (m < p.M)
+            tap_geometry<T>(p, b, oh, ow, t, GM::from_bits(dy[i]), GM::from_bits(dx[i]),
+                            GM::from_bits(mk[i]), packed, wh);
           s_gb[t * kGRows + r] = packed;
           s_gw[t * kGRows + r] = wh;
         }
