@@ -144,6 +144,33 @@ def test_split_in_cuda_graph(cuda):
     _watchdog_clean()
 
 
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+def test_half_sums_that_cancel(cuda, dt):
+    """The K parts hand each other fp32 sums: here each part's sum is ~69000
+    (past fp16's 65504, rounded there by a few tens) while the output, where
+    the two parts cancel, is a few hundred."""
+    B, C, H, W, Cout = 1, 128, 12, 12, 512
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(B, C, H, W, generator=g) * 8.0
+    x[:, :64] += 120.0     # channel chunk 0: K part 0 (18 stages = 2 chunks x 9 taps)
+    x[:, 64:] -= 120.0     # channel chunk 1: K part 1
+    off = torch.zeros(B, 18, H, W)           # integer sample points: exact interpolation
+    mask = torch.ones(B, 9, H, W)
+    w = 1.0 + 0.01 * torch.randn(Cout, C, 3, 3, generator=g)
+    x, off, mask, w = (t.to(cuda, dt) for t in (x, off, mask, w))
+    want = _oracle(x, off, mask, w, None, 1)
+    part0 = _oracle(x[:, :64].contiguous(), off, mask, w[:, :64].contiguous(), None, 1)
+    assert float(part0.abs().max()) > 65520.0
+    x_cl = x.contiguous(memory_format=torch.channels_last)
+    out = torch.full(want.shape, float("nan"), device=cuda, dtype=dt).contiguous(
+        memory_format=torch.channels_last)
+    cabi_dcn_forward(x_cl, off, mask, w, None, out, (1, 1), (1, 1), (1, 1))
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(out).all())
+    assert rel_l2(out, want) <= HALF_REL, rel_l2(out, want)
+    _watchdog_clean()
+
+
 def test_no_split_beyond_one_wave(cuda):
     """Tiles that do not fit in one wave (here 4 x 38 CTAs) take no K split."""
     B, C, H, W, Cout = 4, 256, 40, 60, 512
