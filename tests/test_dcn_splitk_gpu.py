@@ -171,6 +171,36 @@ def test_half_sums_that_cancel(cuda, dt):
     _watchdog_clean()
 
 
+def test_concurrent_calls_on_two_streams(cuda):
+    """Two K-split calls at once on two streams, each with its own workspace:
+    together their clusters exceed one wave, so some CTAs wait for partners
+    that start only when the other call's CTAs finish."""
+    dt = torch.float16
+    B, C, H, W, Cout = 6, 512, 29, 50, 512        # 136 CTAs each: cfg2
+    runs = []
+    for seed in (21, 22):
+        x, off, mask, w, _ = dcn_inputs(seed, B, C, H, W, Cout, off_std=2.0, bias=False)
+        x, off, mask, w = (t.to(cuda, dt) for t in (x, off, mask, w))
+        want = _oracle(x, off, mask, w, None, 1)
+        x = x.contiguous(memory_format=torch.channels_last)
+        out = torch.empty(want.shape, device=cuda, dtype=dt).contiguous(
+            memory_format=torch.channels_last)
+        runs.append((x, off, mask, w, out, want))
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    torch.cuda.synchronize()
+    for rep in range(3):
+        for (x, off, mask, w, out, want), st in zip(runs, streams):
+            out.fill_(float("nan"))
+        torch.cuda.synchronize()
+        for (x, off, mask, w, out, want), st in zip(runs, streams):
+            with torch.cuda.stream(st):
+                cabi_dcn_forward(x, off, mask, w, None, out, (1, 1), (1, 1), (1, 1))
+        torch.cuda.synchronize()
+        for x, off, mask, w, out, want in runs:
+            assert rel_l2(out, want) <= HALF_REL, (rep, rel_l2(out, want))
+    _watchdog_clean()
+
+
 def test_no_split_beyond_one_wave(cuda):
     """Tiles that do not fit in one wave (here 4 x 38 CTAs) take no K split."""
     B, C, H, W, Cout = 4, 256, 40, 60, 512
