@@ -23,7 +23,11 @@
 //   round-robin over a grid of exactly the resident CTAs, so the grid walks
 //   the units in (batch, head, query) order together.
 // * Warp-per-unit kernel (other L*P): the same corner-slot mapping, one unit
-//   per warp, its samples in rounds of 32.
+//   per warp, its samples in rounds of 32.  Its geometry table is corner-major
+//   with two samples' (line, weight) entries per 16-byte word, so the slot's
+//   lanes read two samples' geometry in one shared-memory load (about 1.2
+//   shared-memory wavefronts per sample against 2.1 for separate line and
+//   weight reads), and a batch's corner loads are predicated, not branched.
 // * Any other head dim: one thread per output element.
 // The gather is bound by the 16-byte loads a warp can keep in flight, which
 // the register file caps; batch sizes and CTAs per SM are the measured best.
@@ -92,29 +96,37 @@ __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2hal
 template <>
 __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
-// Geometry of one sample for the four corner slots: line index (pixel*heads +
-// head, relative to the batch's value base) and weight (bilinear * attn; 0 for
-// a dropped corner).
-struct SampleGeom {
-  int idx[4];
-  float w[4];
-};
-
 constexpr int kWarps = 8;
+// Per-warp geometry table of one round of 32 samples, corner-major: corner k's
+// entries are 16 pairs of samples x {line, weight, line, weight}, with a
+// 4-word pad between corners.  Lane s writes its sample's four corners with
+// conflict-free 8-byte stores; the 8 lanes of corner slot g then read two
+// samples' entries in one 16-byte load, the four slots hitting distinct banks.
+constexpr int kGeoCornerWords = 16 * 4 + 4;
+constexpr int kGeoWords = 4 * kGeoCornerWords;
 
+// Predicated vector loads of 4 channels (zeros when `pred` is 0).
+__device__ __forceinline__ uint4 ld_pred16(const void *p, uint32_t pred);
+__device__ __forceinline__ uint2 ld_pred8(const void *p, uint32_t pred);
 template <typename T>
+struct RawVec4;
+
+template <typename T, int BATCH>
 __global__ void __launch_bounds__(kWarps * 32)
 msda_fwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ shapes,
                     const int64_t *__restrict__ lsi, const T *__restrict__ loc,
                     const T *__restrict__ attn, T *__restrict__ out, int S, int heads,
                     int L, int Q, int P, int64_t units) {
+  static_assert(BATCH % 2 == 0 && 32 % BATCH == 0, "BATCH: an even divisor of 32");
   ptx::grid_launch_dependents();
   ptx::grid_wait_prerequisites();
+  using R = RawVec4<T>;
+  using RT = typename R::type;
   using V = Vec4<T>;
   using VT = typename V::type;
   constexpr int C = 32;
   __shared__ int s_lvl[kMaxLevels][3];  // H, W, start
-  __shared__ SampleGeom s_geom[kWarps][32];
+  __shared__ __align__(16) uint32_t s_geo[kWarps][kGeoWords];
 
   if (threadIdx.x < L) {
     s_lvl[threadIdx.x][0] = static_cast<int>(shapes[2 * threadIdx.x]);
@@ -130,20 +142,21 @@ msda_fwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ sha
 
   const int m = static_cast<int>(unit % heads);
   const int64_t b = unit / (static_cast<int64_t>(Q) * heads);
-  const VT *vbase = reinterpret_cast<const VT *>(value + b * S * heads * C);
+  const T *vbase = value + b * S * heads * C;
   const int LP = L * P;
   const T *uloc = loc + unit * LP * 2;
   const T *uattn = attn + unit * LP;
 
   const int g = lane >> 3;  // corner slot
   const int j = lane & 7;   // 4-channel vector within the head's 32 channels
+  const uint32_t geo_s = ptx::smem_u32(&s_geo[warp][0]);
+  const uint32_t my_geo = geo_s + 4u * (g * kGeoCornerWords);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 
   for (int s0 = 0; s0 < LP; s0 += 32) {
     const int s = s0 + lane;
-    SampleGeom geo;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) { geo.idx[k] = 0; geo.w[k] = 0.f; }
+    int idx[4] = {0, 0, 0, 0};
+    float wk[4] = {0.f, 0.f, 0.f, 0.f};
     if (s < LP) {
       const int l = s / P;
       const int Hl = s_lvl[l][0], Wl = s_lvl[l][1], start = s_lvl[l][2];
@@ -162,26 +175,55 @@ msda_fwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ sha
         const bool y0 = h_low >= 0, y1 = h_low + 1 <= Hl - 1;
         const bool x0 = w_low >= 0, x1 = w_low + 1 <= Wl - 1;
         const int base = start + h_low * Wl + w_low;  // pixel of corner (y0, x0)
-        if (y0 && x0) { geo.idx[0] = base * heads + m;            geo.w[0] = hh * hw * a; }
-        if (y0 && x1) { geo.idx[1] = (base + 1) * heads + m;      geo.w[1] = hh * lw * a; }
-        if (y1 && x0) { geo.idx[2] = (base + Wl) * heads + m;     geo.w[2] = lh * hw * a; }
-        if (y1 && x1) { geo.idx[3] = (base + Wl + 1) * heads + m; geo.w[3] = lh * lw * a; }
+        if (y0 && x0) { idx[0] = base * heads + m;            wk[0] = hh * hw * a; }
+        if (y0 && x1) { idx[1] = (base + 1) * heads + m;      wk[1] = hh * lw * a; }
+        if (y1 && x0) { idx[2] = (base + Wl) * heads + m;     wk[2] = lh * hw * a; }
+        if (y1 && x1) { idx[3] = (base + Wl + 1) * heads + m; wk[3] = lh * lw * a; }
       }
     }
-    s_geom[warp][lane] = geo;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t a_s =
+          geo_s + 4u * (k * kGeoCornerWords + (lane >> 1) * 4 + (lane & 1) * 2);
+      asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(a_s), "r"(idx[k]),
+                   "r"(__float_as_uint(wk[k]))
+                   : "memory");
+    }
     __syncwarp();
-    const int n = min(32, LP - s0);
-#pragma unroll 8
-    for (int i = 0; i < n; ++i) {
-      const int idx = s_geom[warp][i].idx[g];
-      const float w = s_geom[warp][i].w[g];
-      if (w != 0.f) {
-        const float4 v = V::to_f32(__ldg(vbase + static_cast<int64_t>(idx) * (C / 4) + j));
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
+    // samples in batches of BATCH: a batch's corner loads are issued together
+    // (predicated off for dropped corners and for entries past the round's
+    // last sample, whose weights are 0), then consumed
+    const int nb = (min(32, LP - s0) + BATCH - 1) / BATCH;
+    for (int bt = 0; bt < nb; ++bt) {
+      RT vb[BATCH];
+      float w[BATCH];
+#pragma unroll
+      for (int k = 0; k < BATCH; k += 2) {
+        const uint4 e = ptx::ld_shared_v4(my_geo + 16u * ((bt * BATCH + k) >> 1));
+        w[k] = __uint_as_float(e.y);
+        w[k + 1] = __uint_as_float(e.w);
+        vb[k] = R::load(vbase + static_cast<int64_t>(static_cast<int>(e.x)) * C + j * 4,
+                        w[k] != 0.f);
+        vb[k + 1] = R::load(vbase + static_cast<int64_t>(static_cast<int>(e.z)) * C + j * 4,
+                            w[k + 1] != 0.f);
       }
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k) {
+        ptx::reg_fence(vb[k]);
+        ptx::reg_fence(w[k]);
+      }
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k) {
+        const float4 v = R::f32(vb[k]);
+        acc.x = fmaf(w[k], v.x, acc.x);
+        acc.y = fmaf(w[k], v.y, acc.y);
+        acc.z = fmaf(w[k], v.z, acc.z);
+        acc.w = fmaf(w[k], v.w, acc.w);
+      }
+      ptx::reg_fence(acc.x);
+      ptx::reg_fence(acc.y);
+      ptx::reg_fence(acc.z);
+      ptx::reg_fence(acc.w);
     }
     __syncwarp();
   }
@@ -518,7 +560,11 @@ int launch_typed(const void *value, const int64_t *shapes, const int64_t *lsi, c
   if (fast) {
     const int64_t blocks = (units + kWarps - 1) / kWarps;
     if (blocks > 0x7FFFFFFF) return fail(BEVK_ERR_INDEX_OVERFLOW, "msda: grid too large");
-    return launched(launch_dependent(msda_fwd_c32_kernel<T>, dim3(static_cast<unsigned>(blocks)),
+    // loads in flight per warp: 16 fp32 or 8 half-width samples (cfg5 on B200:
+    // fp32 480 -> 440 us against the earlier per-corner table, fp16 436 -> 402 us;
+    // fp32 batches of 8 took 458 us, fp16 batches of 16 407 us)
+    const auto kern = sizeof(T) == 4 ? msda_fwd_c32_kernel<T, 16> : msda_fwd_c32_kernel<T, 8>;
+    return launched(launch_dependent(kern, dim3(static_cast<unsigned>(blocks)),
                                      dim3(kWarps * 32), 0, stream, static_cast<const T *>(value),
                                      shapes, lsi, static_cast<const T *>(loc),
                                      static_cast<const T *>(attn), static_cast<T *>(out), S,

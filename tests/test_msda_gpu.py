@@ -92,6 +92,34 @@ def test_large_multilevel_cases(cuda, cfg, dt):
         assert out.dtype == dt and rel_l2(out, want) <= HALF_REL
 
 
+# Multi-level problems outside the pass kernel's L*P (4, 8, 16) on the
+# warp-per-unit kernel: a head count that does not divide the SM count, a
+# small level beside a large one, degenerate levels with two rounds of samples
+# (L*P = 36), and more heads than SMs.  Each case runs twice in a row.
+MULTI = [
+    dict(B=3, shapes=[(36, 64), (18, 32), (9, 16), (5, 8)], M=6, C=32, Q=1200, P=8),
+    dict(B=2, shapes=[(50, 70), (25, 35)], M=8, C=32, Q=800, P=5),
+    dict(B=1, shapes=[(1, 1), (2, 1), (1, 3), (40, 50)], M=8, C=32, Q=600, P=9),
+    dict(B=1, shapes=[(6, 5), (3, 2)], M=160, C=32, Q=20, P=3),
+]
+
+
+@pytest.mark.parametrize("cfg", MULTI, ids=[f"t{i}" for i in range(len(MULTI))])
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16],
+                         ids=["f32", "f16", "bf16"])
+def test_multilevel_warp_per_unit_cases(cuda, cfg, dt):
+    value, shapes, lsi, loc, attn = msda_inputs(13, oob_frac=0.1, **cfg)
+    value, loc, attn = (t.to(cuda, dt) for t in (value, loc, attn))
+    shapes, lsi = shapes.to(cuda), lsi.to(cuda)
+    want = _oracle(value, shapes, lsi, loc, attn)
+    for _ in range(2):
+        out = cabi_msda_forward(value, shapes, lsi, loc, attn)
+        if dt == torch.float32:
+            assert rel_l2(out, want) <= FP32_REL and max_abs(out, want) <= FP32_ABS
+        else:
+            assert out.dtype == dt and rel_l2(out, want) <= HALF_REL
+
+
 @pytest.mark.parametrize("name", ["cfg4", "cfg5"])
 def test_baseline_configs_full_size(cuda, name):
     import ms_deform_attn
