@@ -19,10 +19,11 @@
 // g as 4-channel vectors: one predicated vector load of the corner line, a
 // 4-wide dot with grad_out, and one vector red.global.add.v4.f32 of
 // wk*attn*g into grad_value (a quarter of the reference's per-channel
-// atomics).  The three per-sample sums are folded with shuffles (within a
-// corner group, then across groups), lane s keeps sample s's result and the
-// grad_loc / grad_attn writes of a pass are coalesced.  Loads of a batch of
-// samples are issued before any of them is consumed.  grad_value of fp16 /
+// atomics).  The per-corner dots of a batch of samples are folded by a
+// reduce-scatter inside each corner group, the corners' shares summed with
+// two shuffle rounds, and the grad_loc / grad_attn of a batch written by 8
+// (or 4) lanes.  Loads of a batch of samples are issued before any of them is
+// consumed.  grad_value of fp16 /
 // bf16 problems accumulates in an fp32 workspace and is narrowed at the end,
 // as the reference does (binding_musa.mu:450-507).
 #include <cuda_bf16.h>
@@ -41,7 +42,6 @@ namespace {
 
 constexpr int kMaxLevels = 16;
 constexpr int kBwdWarps = 8;
-constexpr int kBwdBatch = 4;
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v) { return static_cast<float>(v); }
@@ -94,16 +94,25 @@ __device__ __forceinline__ void red_add_v4(float *p, float4 v) {
                : "memory");
 }
 
-struct BwdGeom {
-  long long line0;  // value line (pixel*heads + head, batch included) of corner (h_low, w_low)
-  int row_lines;    // lines between image rows of the level (W_l * heads)
-  int mask;         // in-range bits of corners 0..3 (0 when the sample is dropped)
-  int unit;         // (b, q, m) unit: grad_out line
-  float lh, lw, a;  // fractional position and attention weight
-  float hl, wl;     // H_l, W_l as floats (grad_loc scale)
-};
+// Per-warp geometry table of one pass of 32 samples, corner-major: corner k's
+// entries are 16 pairs of samples x {line, scale, line, scale} (line -1 for a
+// corner outside the level, scale = corner weight x attention weight), with a
+// 4-word pad between corners, so the 8 lanes of corner slot g read two
+// samples' entries in one 16-byte load and the four slots hit distinct banks.
+constexpr int kGeoCornerWords = 16 * 4 + 4;
+constexpr int kGeoWords = 4 * kGeoCornerWords;
 
-template <typename T>
+// BATCH samples are gathered together: their corner loads are issued, then
+// the grad_value reds, then the per-lane partial dots.  The per-corner dots of
+// a batch are folded by a reduce-scatter inside each 8-lane corner group (7
+// shuffles for 8 samples, 4 for 4, where one shuffle per partial sum folded
+// on its own cost 3), leaving lane j of every group with its corner's dot for
+// one sample of the batch; the lane turns it into that corner's shares of
+// grad_attn / grad_loc, and two more rounds of 3 shuffles sum the corners.
+// UNITB: L*P is a multiple of BATCH, so a batch never straddles two (b, q, m)
+// units and one grad_out vector serves the whole batch; otherwise each sample
+// loads its own (an L1 hit for the unit's later samples).
+template <typename T, int BATCH, bool UNITB>
 __global__ void __launch_bounds__(kBwdWarps * 32)
 msda_bwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ shapes,
                     const int64_t *__restrict__ lsi, const T *__restrict__ loc,
@@ -111,11 +120,13 @@ msda_bwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ sha
                     float *__restrict__ grad_value, T *__restrict__ grad_loc,
                     T *__restrict__ grad_attn, int S, int heads, int L, int Q, int P,
                     int64_t n_samples) {
+  static_assert(BATCH == 4 || BATCH == 8, "batches of 4 or 8 samples");
   ptx::grid_launch_dependents();
   ptx::grid_wait_prerequisites();
   constexpr int C = 32;
   __shared__ int s_lvl[kMaxLevels][3];
-  __shared__ BwdGeom s_geo[kBwdWarps][32];
+  __shared__ __align__(16) uint32_t s_geo[kBwdWarps][kGeoWords];
+  __shared__ float4 s_smp[kBwdWarps][32];  // per sample: lh, lw, W_l * a, H_l * a
   if (threadIdx.x < L) {
     s_lvl[threadIdx.x][0] = static_cast<int>(shapes[2 * threadIdx.x]);
     s_lvl[threadIdx.x][1] = static_cast<int>(shapes[2 * threadIdx.x + 1]);
@@ -128,6 +139,8 @@ msda_bwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ sha
   const int g = lane >> 3;  // corner of this lane
   const int j = lane & 7;   // 4-channel chunk
   const int LP = L * P;
+  const uint32_t geo_s = ptx::smem_u32(&s_geo[warp][0]);
+  const uint32_t my_geo = geo_s + 4u * (g * kGeoCornerWords);
   const int64_t passes = (n_samples + 31) / 32;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kBwdWarps;
   for (int64_t ps = static_cast<int64_t>(blockIdx.x) * kBwdWarps + warp; ps < passes;
@@ -135,95 +148,152 @@ msda_bwd_c32_kernel(const T *__restrict__ value, const int64_t *__restrict__ sha
     const int64_t s0 = ps * 32;
     // ---- geometry of sample s0 + lane
     {
-      BwdGeom geo{0, 0, 0, 0, 0.f, 0.f, 0.f, 0.f, 0.f};
+      int line[4] = {-1, -1, -1, -1};
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+      float4 fr = make_float4(0.f, 0.f, 0.f, 0.f);
       const int64_t smp = s0 + lane;
       if (smp < n_samples) {
         const int64_t u = smp / LP;
         const int lp = static_cast<int>(smp - u * LP);
         const int l = lp / P;
         const int m = static_cast<int>(u % heads);
-        const int64_t b = u / (static_cast<int64_t>(Q) * heads);
+        const int b = static_cast<int>(u / (static_cast<int64_t>(Q) * heads));
         const int Hl = s_lvl[l][0], Wl = s_lvl[l][1], start = s_lvl[l][2];
         const float lx = to_f(loc[2 * smp]), ly = to_f(loc[2 * smp + 1]);
+        const float a = to_f(attn[smp]);
         const float h_im = __fmaf_rn(ly, static_cast<float>(Hl), -0.5f);
         const float w_im = __fmaf_rn(lx, static_cast<float>(Wl), -0.5f);
-        geo.unit = static_cast<int>(u);
-        geo.a = to_f(attn[smp]);
-        geo.hl = static_cast<float>(Hl);
-        geo.wl = static_cast<float>(Wl);
-        geo.row_lines = Wl * heads;
+        fr.z = static_cast<float>(Wl) * a;
+        fr.w = static_cast<float>(Hl) * a;
         if (h_im > -1.f && w_im > -1.f && h_im < static_cast<float>(Hl) &&
             w_im < static_cast<float>(Wl)) {
           const int h_low = static_cast<int>(floorf(h_im));
           const int w_low = static_cast<int>(floorf(w_im));
-          geo.lh = h_im - static_cast<float>(h_low);
-          geo.lw = w_im - static_cast<float>(w_low);
+          const float lh = h_im - static_cast<float>(h_low);
+          const float lw = w_im - static_cast<float>(w_low);
+          const float hh = 1.f - lh, hw = 1.f - lw;
+          fr.x = lh;
+          fr.y = lw;
           const bool y0 = h_low >= 0, y1 = h_low + 1 <= Hl - 1;
           const bool x0 = w_low >= 0, x1 = w_low + 1 <= Wl - 1;
-          geo.mask = (y0 && x0 ? 1 : 0) | (y0 && x1 ? 2 : 0) | (y1 && x0 ? 4 : 0) |
-                     (y1 && x1 ? 8 : 0);
-          geo.line0 = (b * S + start + static_cast<int64_t>(h_low) * Wl + w_low) * heads + m;
+          // line of corner (y0, x0): the launcher checks B*S*heads fits 31 bits
+          const int base = (b * S + start + h_low * Wl + w_low) * heads + m;
+          if (y0 && x0) { line[0] = base;                   sc[0] = hh * hw * a; }
+          if (y0 && x1) { line[1] = base + heads;           sc[1] = hh * lw * a; }
+          if (y1 && x0) { line[2] = base + Wl * heads;      sc[2] = lh * hw * a; }
+          if (y1 && x1) { line[3] = base + (Wl + 1) * heads; sc[3] = lh * lw * a; }
         }
       }
-      s_geo[warp][lane] = geo;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t a_s =
+            geo_s + 4u * (k * kGeoCornerWords + (lane >> 1) * 4 + (lane & 1) * 2);
+        asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(a_s), "r"(line[k]),
+                     "r"(__float_as_uint(sc[k]))
+                     : "memory");
+      }
+      s_smp[warp][lane] = fr;
     }
     __syncwarp();
 
-    float my_ga = 0.f, my_gx = 0.f, my_gy = 0.f;  // results of sample s0 + lane
     const int n_here = n_samples - s0 < 32 ? static_cast<int>(n_samples - s0) : 32;
-    for (int i0 = 0; i0 < n_here; i0 += kBwdBatch) {
-      float4 v[kBwdBatch], t[kBwdBatch];
-      long long line[kBwdBatch];
-      uint32_t valid[kBwdBatch];
-#pragma unroll
-      for (int k = 0; k < kBwdBatch; ++k) {
-        const int i = i0 + k < n_here ? i0 + k : n_here - 1;
-        const BwdGeom &geo = s_geo[warp][i];
-        valid[k] = i0 + k < n_here ? (geo.mask >> g) & 1 : 0u;
-        line[k] = geo.line0 + ((g & 1) ? heads : 0) + ((g & 2) ? geo.row_lines : 0);
-        v[k] = Ch4<T>::load(value + line[k] * C + 4 * j, valid[k]);
-        t[k] = Ch4<T>::load(grad_out + static_cast<int64_t>(geo.unit) * C + 4 * j, 1u);
+    // unit of the pass's first sample and the samples left in it (warp-uniform)
+    int64_t u_cur = s0 / LP;
+    int left = LP - static_cast<int>(s0 - u_cur * LP);
+    float4 t_unit = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (UNITB) t_unit = Ch4<T>::load(grad_out + u_cur * C + 4 * j, 1u);
+    for (int i0 = 0; i0 < n_here; i0 += BATCH) {
+      float4 v[BATCH], t[BATCH];
+      int ln[BATCH];
+      float sc[BATCH];
+      if (UNITB) {
+        if (left == 0) {
+          ++u_cur;
+          left = LP;
+          t_unit = Ch4<T>::load(grad_out + u_cur * C + 4 * j, 1u);
+        }
+        left -= BATCH;
       }
 #pragma unroll
-      for (int k = 0; k < kBwdBatch; ++k) {
-        if (i0 + k >= n_here) break;
-        const BwdGeom &geo = s_geo[warp][i0 + k];
-        const float lh = geo.lh, lw = geo.lw, hh = 1.f - lh, hw = 1.f - lw;
-        // corner weight and its derivatives along w and h
-        const float wk = g == 0 ? hh * hw : g == 1 ? hh * lw : g == 2 ? lh * hw : lh * lw;
-        const float cx = g == 0 ? -hh : g == 1 ? hh : g == 2 ? -lh : lh;
-        const float cy = g == 0 ? -hw : g == 1 ? -lw : g == 2 ? hw : lw;
-        if (valid[k]) {
-          const float s = wk * geo.a;
-          red_add_v4(grad_value + line[k] * C + 4 * j,
-                     make_float4(s * t[k].x, s * t[k].y, s * t[k].z, s * t[k].w));
+      for (int k = 0; k < BATCH; k += 2) {
+        const uint4 e = ptx::ld_shared_v4(my_geo + 16u * ((i0 + k) >> 1));
+        ln[k] = static_cast<int>(e.x);
+        sc[k] = __uint_as_float(e.y);
+        ln[k + 1] = static_cast<int>(e.z);
+        sc[k + 1] = __uint_as_float(e.w);
+      }
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k) {
+        v[k] = Ch4<T>::load(value + static_cast<int64_t>(ln[k]) * C + 4 * j, ln[k] >= 0);
+        if (!UNITB) {
+          const bool here = i0 + k < n_here;
+          if (here && left == 0) {
+            ++u_cur;
+            left = LP;
+          }
+          left -= here ? 1 : 0;
+          t[k] = Ch4<T>::load(grad_out + u_cur * C + 4 * j, here);
+        } else {
+          t[k] = t_unit;
         }
+      }
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k) {
+        if (sc[k] != 0.f)  // a dropped corner and a zero weight add nothing
+          red_add_v4(grad_value + static_cast<int64_t>(ln[k]) * C + 4 * j,
+                     make_float4(sc[k] * t[k].x, sc[k] * t[k].y, sc[k] * t[k].z,
+                                 sc[k] * t[k].w));
+      }
+      float p[BATCH];
+#pragma unroll
+      for (int k = 0; k < BATCH; ++k) {
         float d = v[k].x * t[k].x;
         d = fmaf(v[k].y, t[k].y, d);
         d = fmaf(v[k].z, t[k].z, d);
-        d = fmaf(v[k].w, t[k].w, d);
-        d += __shfl_xor_sync(0xffffffffu, d, 1);  // the corner's 32-channel dot
-        d += __shfl_xor_sync(0xffffffffu, d, 2);
-        d += __shfl_xor_sync(0xffffffffu, d, 4);
-        float qa = wk * d, qx = cx * d, qy = cy * d;
-#pragma unroll
-        for (int o = 8; o <= 16; o <<= 1) {  // across the four corners
-          qa += __shfl_xor_sync(0xffffffffu, qa, o);
-          qx += __shfl_xor_sync(0xffffffffu, qx, o);
-          qy += __shfl_xor_sync(0xffffffffu, qy, o);
-        }
-        if (lane == i0 + k) {
-          my_ga = qa;
-          my_gx = geo.wl * geo.a * qx;
-          my_gy = geo.hl * geo.a * qy;
-        }
+        p[k] = fmaf(v[k].w, t[k].w, d);
       }
-    }
-    if (lane < n_here) {
-      const int64_t smp = s0 + lane;
-      grad_attn[smp] = from_f<T>(my_ga);
-      grad_loc[2 * smp] = from_f<T>(my_gx);
-      grad_loc[2 * smp + 1] = from_f<T>(my_gy);
+      // reduce-scatter over the 8 lanes of the corner group
+      constexpr int H1 = BATCH / 2, H2 = BATCH / 4;
+      const bool b2 = (j & 4) != 0, b1 = (j & 2) != 0, b0 = (j & 1) != 0;
+      float q1[H1], q2[H2];
+#pragma unroll
+      for (int i = 0; i < H1; ++i) {
+        const float send = b2 ? p[i] : p[i + H1];
+        q1[i] = (b2 ? p[i + H1] : p[i]) + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+#pragma unroll
+      for (int i = 0; i < H2; ++i) {
+        const float send = b1 ? q1[i] : q1[i + H2];
+        q2[i] = (b1 ? q1[i + H2] : q1[i]) + __shfl_xor_sync(0xffffffffu, send, 2);
+      }
+      float D;
+      int si;  // sample of the batch whose corner-g dot this lane now holds
+      if constexpr (BATCH == 8) {
+        const float send = b0 ? q2[0] : q2[1];
+        D = (b0 ? q2[1] : q2[0]) + __shfl_xor_sync(0xffffffffu, send, 1);
+        si = i0 + j;
+      } else {
+        D = q2[0] + __shfl_xor_sync(0xffffffffu, q2[0], 1);
+        si = i0 + (j >> 1);
+      }
+      const float4 fr = s_smp[warp][si];
+      const float wy = (g & 2) ? fr.x : 1.f - fr.x;  // lh or hh
+      const float wx = (g & 1) ? fr.y : 1.f - fr.y;  // lw or hw
+      float qa = wy * wx * D;
+      float qx = ((g & 1) ? wy : -wy) * D;
+      float qy = ((g & 2) ? wx : -wx) * D;
+#pragma unroll
+      for (int o = 8; o <= 16; o <<= 1) {  // across the four corners
+        qa += __shfl_xor_sync(0xffffffffu, qa, o);
+        qx += __shfl_xor_sync(0xffffffffu, qx, o);
+        qy += __shfl_xor_sync(0xffffffffu, qy, o);
+      }
+      if (g == 0 && (BATCH == 8 || !b0) && si < n_here) {
+        const int64_t smp = s0 + si;
+        grad_attn[smp] = from_f<T>(qa);
+        grad_loc[2 * smp] = from_f<T>(fr.z * qx);
+        grad_loc[2 * smp + 1] = from_f<T>(fr.w * qy);
+      }
     }
     __syncwarp();
   }
@@ -324,13 +394,18 @@ int launch_bwd_typed(const void *value, const int64_t *shapes, const int64_t *ls
     const int sms = device_info(current_device()).sm_count;
     const bool fast = C == 32 && L <= kMaxLevels && aligned(value, sizeof(T) * 4) &&
                       aligned(grad_out, sizeof(T) * 4) && aligned(gv, 16) &&
-                      static_cast<int64_t>(B) * Q * heads < (int64_t(1) << 31);
+                      static_cast<int64_t>(B) * Q * heads < (int64_t(1) << 31) &&
+                      static_cast<int64_t>(B) * S * heads < (int64_t(1) << 31);
     if (fast) {
       const int64_t passes = (n_samples + 31) / 32;
       const int64_t want = (passes + kBwdWarps - 1) / kBwdWarps;
       const int64_t ctas = std::min<int64_t>(want, static_cast<int64_t>(sms > 0 ? sms : 148) * 8);
+      const int LP = L * P;
+      const auto kern = LP % 8 == 0   ? msda_bwd_c32_kernel<T, 8, true>
+                        : LP % 4 == 0 ? msda_bwd_c32_kernel<T, 4, true>
+                                      : msda_bwd_c32_kernel<T, 4, false>;
       const int st = launched(
-          launch_dependent(msda_bwd_c32_kernel<T>, dim3(static_cast<unsigned>(ctas)),
+          launch_dependent(kern, dim3(static_cast<unsigned>(ctas)),
                            dim3(kBwdWarps * 32), 0, stream, static_cast<const T *>(value), shapes,
                            lsi, static_cast<const T *>(loc), static_cast<const T *>(attn),
                            static_cast<const T *>(grad_out), gv, static_cast<T *>(grad_loc),
