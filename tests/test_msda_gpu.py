@@ -179,6 +179,19 @@ def test_backward_small_cases(cuda, cfg, dt):
     _check_grads(cabi_msda_backward(value, shapes, lsi, loc, attn, gout), want, dt)
 
 
+# The multi-level cases through the backward: L*P = 32 (batches of 8 sharing
+# one grad_out vector), 10 and 6 (batches of 4 that cross unit boundaries,
+# one grad_out vector per sample) and 36 (batches of 4 inside a unit), with
+# passes of 32 samples that start mid-unit.
+@pytest.mark.parametrize("cfg", MULTI, ids=[f"t{i}" for i in range(len(MULTI))])
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16, torch.bfloat16],
+                         ids=["f32", "f16", "bf16"])
+def test_backward_multilevel_cases(cuda, cfg, dt):
+    value, shapes, lsi, loc, attn, gout = _bwd_case(cuda, cfg, dt, seed=17)
+    want = _oracle_bwd(value, shapes, lsi, loc, attn, gout)
+    _check_grads(cabi_msda_backward(value, shapes, lsi, loc, attn, gout), want, dt)
+
+
 @pytest.mark.parametrize("name", ["cfg4", "cfg5"])
 def test_backward_baseline_configs_full_size(cuda, name):
     import ms_deform_attn
