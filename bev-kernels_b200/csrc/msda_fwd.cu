@@ -21,7 +21,9 @@
 //   keeps a 4-channel partial sum for its corner slot; the slots of a unit are
 //   folded with two shuffles when its last sample is done.  Passes are dealt
 //   round-robin over a grid of exactly the resident CTAs, so the grid walks
-//   the units in (batch, head, query) order together.
+//   the units in (batch, head, query) order together.  A warp's passes are a
+//   fixed number of units apart, so each lane advances its (batch, head,
+//   query) by that stride with carries instead of dividing per pass.
 // * Warp-per-unit kernel (other L*P): the same corner-slot mapping, one unit
 //   per warp, its samples in rounds of 32.  Its geometry table is corner-major
 //   with two samples' (line, weight) entries per 16-byte word, so the slot's
@@ -327,20 +329,35 @@ msda_fwd_pass_kernel(const T *__restrict__ value, const int64_t *__restrict__ sh
   const int64_t HQ = static_cast<int64_t>(heads) * Q;
   const int my_l = (lane % LP) / P;  // level of this lane's sample (fixed across passes)
 
-  // unit v (in (b, h, q) order) of this lane's sample in pass `ps`
-  auto unit_of = [&](int64_t ps, int64_t &b, int &h, int64_t &q) {
-    const int64_t v = ps * UPP + lane / LP;
-    b = v / HQ;
-    const int64_t r = v - b * HQ;
-    h = static_cast<int>(r / Q);
-    q = r - static_cast<int64_t>(h) * Q;
+  // Unit (b, h, q) of this lane's sample, in (b, h, q) order.  A warp's
+  // passes are p_stride apart, i.e. a fixed number of units, so the position
+  // of the next pass is the current one plus that stride's (b, h, q) with
+  // carries: one division per thread at the start instead of two 64-bit
+  // divisions per pass.
+  struct UPos {
+    int b, h, q;
   };
-  // raw location / attention of this lane's sample in pass `ps`
-  auto fetch = [&](int64_t ps, float &lx, float &ly, float &a) {
-    int64_t b, q;
-    int h;
-    unit_of(ps, b, h, q);
-    const int64_t u = (b * Q + q) * heads + h;  // memory order (b, q, h)
+  auto decompose = [&](int64_t v) {
+    UPos r;
+    r.b = static_cast<int>(v / HQ);
+    const int64_t rr = v - static_cast<int64_t>(r.b) * HQ;
+    r.h = static_cast<int>(rr / Q);
+    r.q = static_cast<int>(rr - static_cast<int64_t>(r.h) * Q);
+    return r;
+  };
+  const UPos step = decompose(p_stride * UPP);
+  auto advance = [&](UPos &u) {
+    u.q += step.q;
+    int c = u.q >= Q ? 1 : 0;
+    u.q -= c ? Q : 0;
+    u.h += step.h + c;
+    c = u.h >= heads ? 1 : 0;
+    u.h -= c ? heads : 0;
+    u.b += step.b + c;
+  };
+  // raw location / attention of this lane's sample at unit position `up`
+  auto fetch = [&](const UPos &up, float &lx, float &ly, float &a) {
+    const int64_t u = (static_cast<int64_t>(up.b) * Q + up.q) * heads + up.h;  // memory order (b, q, h)
     const int i = lane % LP;
     lx = to_f32(loc[(u * LP + i) * 2]);
     ly = to_f32(loc[(u * LP + i) * 2 + 1]);
@@ -348,12 +365,14 @@ msda_fwd_pass_kernel(const T *__restrict__ value, const int64_t *__restrict__ sh
   };
 
   float lx = 0.f, ly = 0.f, a = 0.f;
-  if (p_first < passes) fetch(p_first, lx, ly, a);
+  UPos nxt = decompose(p_first * UPP + lane / LP);
+  if (p_first < passes) fetch(nxt, lx, ly, a);
   for (int64_t ps = p_first; ps < passes; ps += p_stride) {
     // ---- geometry of this pass (lane = sample)
-    int64_t b, q;
-    int h;
-    unit_of(ps, b, h, q);
+    const UPos cur = nxt;
+    advance(nxt);
+    const int64_t b = cur.b, q = cur.q;
+    const int h = cur.h;
     {
       const int Hl = s_lvl[my_l][0], Wl = s_lvl[my_l][1], start = s_lvl[my_l][2];
       CornerGeom cg[4] = {{0, 0.f}, {0, 0.f}, {0, 0.f}, {0, 0.f}};
@@ -385,7 +404,7 @@ msda_fwd_pass_kernel(const T *__restrict__ value, const int64_t *__restrict__ sh
     }
     __syncwarp();
     // next pass's raw inputs are loaded while this pass gathers
-    if (ps + p_stride < passes) fetch(ps + p_stride, lx, ly, a);
+    if (ps + p_stride < passes) fetch(nxt, lx, ly, a);
 
     // ---- gather: batches of BATCH samples
     RT buf[DB ? 2 : 1][BATCH];
