@@ -18,8 +18,8 @@
 //   being loaded.  Each sample then costs the warp ONE load instruction
 //   covering all four corners: lanes 8g..8g+7 read corner g's 32-channel line
 //   as 4-channel vectors, predicated (no branches), in batches.  Each lane
-//   keeps a 4-channel partial sum for its corner slot; the slots of a unit are
-//   folded with two shuffles when its last sample is done.  Passes are dealt
+//   keeps a 4-channel partial sum for its corner slot; the slots of two
+//   consecutive units are folded together when the second one is done.  Passes are dealt
 //   round-robin over a grid of exactly the resident CTAs, so the grid walks
 //   the units in (batch, head, query) order together.  A warp's passes are a
 //   fixed number of units apart, so each lane advances its (batch, head,
@@ -300,6 +300,7 @@ msda_fwd_pass_kernel(const T *__restrict__ value, const int64_t *__restrict__ sh
   static_assert(32 % LP == 0, "LP must divide 32");
   constexpr int C = 32;
   constexpr int UPP = 32 / LP;  // units per pass
+  static_assert(UPP % 2 == 0, "units are folded in pairs");
   using R = RawVec4<T>;
   using RT = typename R::type;
   using V = Vec4<T>;
@@ -422,6 +423,26 @@ msda_fwd_pass_kernel(const T *__restrict__ value, const int64_t *__restrict__ sh
       }
     };
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    // The corner slots of two consecutive units are folded together: the
+    // lane halves exchange one unit each (xor 16), then the quarters finish
+    // (xor 8) -- 8 shuffles for two units where folding each alone takes 16;
+    // slots 0 and 2 then hold units 0 and 1 (cfg4 fp32 102 -> 96 us, fp16 92
+    // -> 81 us on B200; folding four units at once spilled and took 97 / 85).
+    float4 held[2];
+    auto fold_store = [&](int u0) {
+      const bool hi = (g & 2) != 0;
+      auto xr = [](float4 v, int o) {
+        return make_float4(__shfl_xor_sync(0xffffffffu, v.x, o), __shfl_xor_sync(0xffffffffu, v.y, o),
+                           __shfl_xor_sync(0xffffffffu, v.z, o), __shfl_xor_sync(0xffffffffu, v.w, o));
+      };
+      auto add = [](float4 a, float4 b) {
+        return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+      };
+      float4 r = add(hi ? held[1] : held[0], xr(hi ? held[0] : held[1], 16));
+      r = add(r, xr(r, 8));
+      if ((g & 1) == 0)
+        reinterpret_cast<VT *>(out + s_obase[warp][u0 + (hi ? 1 : 0)])[j] = V::from_f32(r);
+    };
     auto consume = [&](int bt, RT (&vb)[BATCH], float (&wb)[BATCH]) {
 #pragma unroll
       for (int k = 0; k < BATCH; ++k) {
@@ -436,17 +457,11 @@ msda_fwd_pass_kernel(const T *__restrict__ value, const int64_t *__restrict__ sh
         acc.y = fmaf(wb[k], v.y, acc.y);
         acc.z = fmaf(wb[k], v.z, acc.z);
         acc.w = fmaf(wb[k], v.w, acc.w);
-        if ((smp + 1) % LP == 0) {  // last sample of a unit: fold corner slots, store
-#pragma unroll
-          for (int o = 8; o <= 16; o <<= 1) {
-            acc.x += __shfl_xor_sync(0xffffffffu, acc.x, o);
-            acc.y += __shfl_xor_sync(0xffffffffu, acc.y, o);
-            acc.z += __shfl_xor_sync(0xffffffffu, acc.z, o);
-            acc.w += __shfl_xor_sync(0xffffffffu, acc.w, o);
-          }
-          if (g == 0)
-            reinterpret_cast<VT *>(out + s_obase[warp][smp / LP])[j] = V::from_f32(acc);
+        if ((smp + 1) % LP == 0) {  // last sample of a unit
+          const int uu = smp / LP;   // unit within the pass (compile-time after unrolling)
+          held[uu % 2] = acc;
           acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (uu % 2 == 1) fold_store(uu - 1);
         }
       }
     };
