@@ -102,6 +102,43 @@ __device__ __forceinline__ uint32_t half2_as_u32(__half2 h) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// Packed pairs of fp16 or bf16 in 32-bit words: a weight broadcast to both
+// halves, a * b, and a * b + c, each rounded to the type.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2_weight(float w) {
+  if constexpr (std::is_same_v<T, __half>) {
+    return half2_as_u32(__float2half2_rn(w));
+  } else {
+    const __nv_bfloat162 h = __float2bfloat162_rn(w);
+    return *reinterpret_cast<const uint32_t *>(&h);
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+  if constexpr (std::is_same_v<T, __half>) {
+    return half2_as_u32(__hmul2(u32_as_half2(a), u32_as_half2(b)));
+  } else {
+    __nv_bfloat162 x, y;
+    *reinterpret_cast<uint32_t *>(&x) = a;
+    *reinterpret_cast<uint32_t *>(&y) = b;
+    const __nv_bfloat162 r = __hmul2(x, y);
+    return *reinterpret_cast<const uint32_t *>(&r);
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint32_t fma2(uint32_t a, uint32_t b, uint32_t c) {
+  if constexpr (std::is_same_v<T, __half>) {
+    return half2_as_u32(__hfma2(u32_as_half2(a), u32_as_half2(b), u32_as_half2(c)));
+  } else {
+    __nv_bfloat162 x, y, z;
+    *reinterpret_cast<uint32_t *>(&x) = a;
+    *reinterpret_cast<uint32_t *>(&y) = b;
+    *reinterpret_cast<uint32_t *>(&z) = c;
+    const __nv_bfloat162 r = __hfma2(x, y, z);
+    return *reinterpret_cast<const uint32_t *>(&r);
+  }
+}
+
 // d0 += a.lo * b.lo, d1 += a.hi * b.hi for channel pair i of two 16-byte
 // vectors.  fp16 / bf16 operands go straight from their packed words into
 // mixed-precision FMAs (the product of two 16-bit floats is exact in fp32, so
@@ -408,9 +445,9 @@ dcn_bwd_sample_kernel(const BwdDataParams p, const T *__restrict__ x, const T *_
       xo[k] = valid[k] ? y * p.xs2 + xx * p.xs3 : 0;
       wm[k] = wk[k] * m0;  // the forward's corner weight, mask folded in
     }
-    __half2 w2[4];  // fp16 path: the weights as packed halves
+    uint32_t w2[4];  // 16-bit paths: the weights as packed pairs of the input type
 #pragma unroll
-    for (int k = 0; k < 4; ++k) w2[k] = __float2half2_rn(wm[k]);
+    for (int k = 0; k < 4; ++k) w2[k] = pack2_weight<T>(wm[k]);
     const bool load_d = coord && h0 != kOutside;
     const T *dc_row = dcol + row_d + static_cast<int64_t>(t0 + j) * p.C;
     T *col_row = col != nullptr ? col + row_c + static_cast<int64_t>(t0 + j) * p.C : nullptr;
@@ -426,19 +463,19 @@ dcn_bwd_sample_kernel(const BwdDataParams p, const T *__restrict__ x, const T *_
                          : make_uint4(0, 0, 0, 0);
       const uint4 dr = load_d ? __ldg(reinterpret_cast<const uint4 *>(dc_row + c))
                               : make_uint4(0, 0, 0, 0);
-      if constexpr (std::is_same_v<T, __half>) {
-        // fp16: the column values as the fused forward kernel builds its A
-        // tiles -- fp16 corner weights (mask folded in), a packed half2
-        // multiply and three FMAs per channel pair -- so no operand is
-        // converted to fp32 in this loop (the corner sums take the packed
-        // words directly)
+      if constexpr (sizeof(T) == 2) {
+        // fp16 / bf16: the column values as the fused forward kernel builds
+        // its A tiles -- corner weights in the input type (mask folded in), a
+        // packed multiply and three packed FMAs per channel pair, each step
+        // rounded to the input type -- so no operand is converted to fp32 in
+        // this loop (the corner sums take the packed words directly)
         uint32_t cw[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          __half2 r = __hmul2(w2[0], u32_as_half2(word(xr[0], i)));
+          uint32_t r = mul2<T>(w2[0], word(xr[0], i));
 #pragma unroll
-          for (int k = 1; k < 4; ++k) r = __hfma2(w2[k], u32_as_half2(word(xr[k], i)), r);
-          cw[i] = half2_as_u32(r);
+          for (int k = 1; k < 4; ++k) r = fma2<T>(w2[k], word(xr[k], i), r);
+          cw[i] = r;
 #pragma unroll
           for (int k = 0; k < 4; ++k) fma_pair<T>(D[k].x, D[k].y, dr, xr[k], i);
         }

@@ -428,7 +428,7 @@ msda_fwd_pass_kernel(const T *__restrict__ value, const int64_t *__restrict__ sh
     // (xor 8) -- 8 shuffles for two units where folding each alone takes 16;
     // slots 0 and 2 then hold units 0 and 1 (cfg4 fp32 102 -> 96 us, fp16 92
     // -> 81 us on B200; folding four units at once spilled and took 97 / 85).
-    float4 held[2];
+    float4 held[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
     auto fold_store = [&](int u0) {
       const bool hi = (g & 2) != 0;
       auto xr = [](float4 v, int o) {

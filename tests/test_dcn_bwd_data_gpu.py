@@ -4,9 +4,12 @@ CPU oracle's DCN backward, and its column matrix against bevk_dcn_columns.
 
 Tolerances: fp32 within 1e-5 relative L2; fp16/bf16 within 5e-3 relative L2 of
 the fp32 oracle on the up-cast inputs; the column matrix bit-identical to the
-im2col kernel's for fp32 and bf16 (fp32 interpolation, rounded once), within
-2e-3 relative L2 of it for fp16 (built as the fused forward builds its
-tiles: fp16 weights, packed half2 FMAs).
+im2col kernel's for fp32 (fp32 interpolation, rounded once), and for fp16 /
+bf16 built as the fused forward builds its tiles (weights in the input type,
+a packed multiply and three packed FMAs, each step rounded to the type):
+within 2e-3 relative L2 of the im2col kernel's for fp16 and 1e-2 for bf16
+(an 8-bit mantissa rounded four times; grad_weight, which sums the column
+matrix over the pixels, is checked against the oracle at 5e-3 elsewhere).
 """
 import ctypes
 
@@ -78,6 +81,8 @@ def test_matches_oracle(cuda, case, dt):
         assert rel_l2(g, torch.from_numpy(ref)) <= tol, (name, rel_l2(g, torch.from_numpy(ref)))
     if dt == torch.float16:
         assert rel_l2(col, ref_col) <= 2e-3, rel_l2(col, ref_col)
+    elif dt == torch.bfloat16:
+        assert rel_l2(col, ref_col) <= 1e-2, rel_l2(col, ref_col)
     else:
         assert torch.equal(col, ref_col)
 
