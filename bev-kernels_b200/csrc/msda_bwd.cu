@@ -23,9 +23,9 @@
 // reduce-scatter inside each corner group, the corners' shares summed with
 // two shuffle rounds, and the grad_loc / grad_attn of a batch written by 8
 // (or 4) lanes.  Loads of a batch of samples are issued before any of them is
-// consumed.  grad_value of fp16 /
-// bf16 problems accumulates in an fp32 workspace and is narrowed at the end,
-// as the reference does (binding_musa.mu:450-507).
+// consumed.  grad_value of fp16 / bf16 problems accumulates in an fp32
+// workspace and is narrowed at the end, as the reference does
+// (binding_musa.mu:450-507).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
