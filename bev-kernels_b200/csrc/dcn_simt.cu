@@ -20,6 +20,7 @@
 #include <cstdint>
 
 #include "bevk_internal.h"
+#include "bevk_ptx.cuh"
 
 namespace bevk {
 namespace {
@@ -219,8 +220,12 @@ dcn_fwd_simt_kernel(SimtParams p, const T *__restrict__ x, const T *__restrict__
 // Cin_g <= 64); the geometry of every (tap, deformable group) of the CTA's
 // pixels is computed once up front; and the next chunk's samples and weights
 // are loaded into registers while the current chunk's products accumulate, so
-// each chunk costs about one global-memory latency.  Same arithmetic as the
-// large kernel (fp32/fp64 sampling, Acc accumulation), same results.
+// each chunk costs about one global-memory latency.  With three or more taps
+// and few tiles, the taps are split over a cluster of 3 CTAs (grid z), each
+// walking a third of the chunks; rank 0 adds the other two partial tiles,
+// read through distributed shared memory in rank order, before the epilogue.
+// Same sampling arithmetic as the large kernel (fp32/fp64, Acc accumulation);
+// the sum over the taps is grouped in thirds.
 constexpr int SBM = 16, SBK = 64;
 constexpr int kSmallA = SBM * SBK / NT;   // gathered samples a thread loads per chunk
 constexpr int kSmallB = BN * SBK / NT;    // weights a thread loads per chunk
@@ -249,12 +254,19 @@ dcn_fwd_simt_small_kernel(SimtParams p, const T *__restrict__ x, const T *__rest
   const int c_base = grp * p.Cin_g;
   const bool cl = p.xs[1] == 1;   // channel-contiguous input: channels fastest across threads
 
-  // geometry of every (tap, deformable group) x pixel of this tile
+  // K split across a cluster of gridDim.z CTAs: CTA z walks taps
+  // [t_lo, t_hi) and the cluster's partial tiles are summed at the end
+  const int ks = static_cast<int>(gridDim.z);
+  const int t_lo = p.T * static_cast<int>(blockIdx.z) / ks;
+  const int t_hi = p.T * (static_cast<int>(blockIdx.z) + 1) / ks;
+
+  // geometry of every (tap, deformable group) x pixel of this tile (of the
+  // CTA's taps)
   const int n_geo = p.T * (p.Cin / p.cpdg);   // taps x deformable groups
   for (int e = tid; e < n_geo * SBM; e += NT) {
     const int tg = e / SBM, r = e - (e / SBM) * SBM;
     const int t = tg % p.T, dgi = tg / p.T;
-    s_geo[e] = tap_geometry<Acc>(p, off, msk, m0 + r, t, dgi);
+    if (t >= t_lo && t < t_hi) s_geo[e] = tap_geometry<Acc>(p, off, msk, m0 + r, t, dgi);
   }
   __syncthreads();
 
@@ -271,7 +283,7 @@ dcn_fwd_simt_small_kernel(SimtParams p, const T *__restrict__ x, const T *__rest
   };
   auto next_chunk = [&](Chunk c, bool &more) {
     if (c.c1 < p.Cin_g) return chunk_at(c.t, c.c1);
-    if (c.t + 1 < p.T) return chunk_at(c.t + 1, 0);
+    if (c.t + 1 < t_hi) return chunk_at(c.t + 1, 0);
     more = false;
     return c;
   };
@@ -334,7 +346,7 @@ dcn_fwd_simt_small_kernel(SimtParams p, const T *__restrict__ x, const T *__rest
   };
 
   Acc acc[4] = {Acc(0), Acc(0), Acc(0), Acc(0)};
-  Chunk cur = chunk_at(0, 0);
+  Chunk cur = chunk_at(t_lo, 0);
   load(cur);
   store(0);
   __syncthreads();
@@ -354,6 +366,37 @@ dcn_fwd_simt_small_kernel(SimtParams p, const T *__restrict__ x, const T *__rest
     __syncthreads();
     buf ^= 1;
     cur = nxt;
+  }
+
+  if (ks > 1) {
+    // partial tiles through distributed shared memory: every CTA leaves its
+    // sums in its A buffers, rank 0 adds the others' in rank order (so the
+    // result does not depend on timing) and writes the output; the second
+    // barrier keeps the other CTAs resident until rank 0 has read them
+    Acc *part = reinterpret_cast<Acc *>(simt_small_smem);
+    static_assert(SBM * BN * sizeof(Acc) <= 2 * sizeof(ATile), "partial tile fits the A buffers");
+    __syncthreads();  // every thread is done reading the chunk buffers
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) part[ty * BN + tx * 4 + jj] = acc[jj];
+    ptx::cluster_sync();
+    if (ptx::cluster_ctarank() == 0) {
+      for (int r = 1; r < ks; ++r) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const uint32_t a = ptx::mapa_shared(ptx::smem_u32(&part[ty * BN + tx * 4 + jj]),
+                                              static_cast<uint32_t>(r));
+          Acc v;
+          if constexpr (sizeof(Acc) == 8) {
+            asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(a) : "memory");
+          } else {
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+          }
+          acc[jj] += v;
+        }
+      }
+    }
+    ptx::cluster_sync();
+    if (ptx::cluster_ctarank() != 0) return;
   }
 
   const int64_t m = m0 + ty;
@@ -561,11 +604,30 @@ int launch_simt_typed(const bevk_dcn_problem *pr, const DcnDims &d, const void *
       if (dev >= 0 && dev < kMaxDevices) sized[dev].store(true, std::memory_order_relaxed);
     }
     const int64_t smt = (d.M + SBM - 1) / SBM;
-    dim3 sgrid(static_cast<unsigned>(smt), static_cast<unsigned>(nt));
-    dcn_fwd_simt_small_kernel<T, Acc><<<sgrid, NT, smem, stream>>>(
-        p, static_cast<const T *>(x), static_cast<const T *>(off), static_cast<const T *>(msk),
-        static_cast<const T *>(wpk), static_cast<const T *>(bias), static_cast<T *>(y));
-    return check_launch("dcn_fwd_simt_small_kernel");
+    // The taps are split over a cluster of 3 CTAs when the tiles are few:
+    // each CTA's chain of dependent chunks (one global round trip each) is
+    // then a third as long (1 x 64 x 32 x 32 fp32: 64 tiles x 9 taps, 35.5 ->
+    // 22.3 us on B200); the partial tiles are summed over distributed shared
+    // memory in a fixed order
+    constexpr int kSplit = 3;
+    const int ks = d.T >= kSplit && smt * nt * kSplit <= 4 * static_cast<int64_t>(sms) ? kSplit : 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(smt), static_cast<unsigned>(nt), static_cast<unsigned>(ks));
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = static_cast<unsigned>(ks);
+    cfg.attrs = attr;
+    cfg.numAttrs = ks > 1 ? 1 : 0;
+    return launched(cudaLaunchKernelEx(&cfg, dcn_fwd_simt_small_kernel<T, Acc>, p,
+                                       static_cast<const T *>(x), static_cast<const T *>(off),
+                                       static_cast<const T *>(msk), static_cast<const T *>(wpk),
+                                       static_cast<const T *>(bias), static_cast<T *>(y)),
+                    "dcn_fwd_simt_small_kernel");
   }
   dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt));
   dcn_fwd_simt_kernel<T, Acc><<<grid, NT, 0, stream>>>(
