@@ -199,6 +199,31 @@ def test_fp32_simt_kernels(cuda, case):
     assert rel_l2(out, want) <= FP32_REL and max_abs(out, want) <= FP32_ABS
 
 
+# Kernel shapes for the small-tile kernel's tap split (three CTAs of a cluster
+# take a third of the taps each when there are at least three): 1 x 2 (no
+# split), 1 x 4 and 1 x 5 (uneven thirds), 2 x 2 with deformable groups, in
+# fp32 and fp64.
+TAP_SPLIT_CASES = [
+    ((1, 2), (0, 1), 1, torch.float32),
+    ((1, 4), (0, 2), 1, torch.float32),
+    ((1, 5), (0, 2), 1, torch.float64),
+    ((2, 2), (1, 1), 2, torch.float32),
+]
+
+
+@pytest.mark.parametrize("case", TAP_SPLIT_CASES, ids=["k1x2", "k1x4", "k1x5_f64", "k2x2_dg2"])
+def test_small_kernel_tap_split_shapes(cuda, case):
+    k, pad, dg, dt = case
+    x, off, mask, w, b = dcn_inputs(23, 1, 32, 14, 18, 48, k=k, pad=pad, dg=dg, off_std=1.5)
+    want = _oracle(x, off, mask, w, b, (1, 1), pad, (1, 1), dg=dg)
+    x, off, mask, w, b = (t.to(cuda, dt) for t in (x, off, mask, w, b))
+    out = torch.full(want.shape, float("nan"), device=cuda, dtype=dt)
+    for _ in range(2):  # the second call overwrites the first's output in full
+        cabi_dcn_forward(x, off, mask, w, b, out, (1, 1), pad, (1, 1), dg=dg)
+        torch.cuda.synchronize()
+        assert rel_l2(out, want) <= FP32_REL and max_abs(out, want) <= FP32_ABS
+
+
 def test_im2col_compat_ops(cuda):
     """Reference extension column ops vs the reference goldens' column matrices."""
     import _modulated_deform_conv_ext as ext
